@@ -1,0 +1,158 @@
+/*
+ * tqkv.h — C ABI of the B200 INT8 KV-cache decode path.
+ *
+ * Plain C: every argument is a pointer, a size or a stream; every entry point
+ * returns a tqkv_status and never aborts.  The C++ launchers that keep the
+ * reference's exact signatures (attention.h, quantization.h) are thin shims
+ * over these functions.
+ *
+ * Layouts (identical to the reference, quantization.h:5-12 of the reference):
+ *   Q, O       : fp16 [B, H, D]
+ *   K, V       : fp16 [B, H, S, D]
+ *   Kq, Vq     : int8 [B, H, S, D]
+ *   Ks, Vs     : fp16 [B, H, S, D / block_size]
+ * fp16 tensors are passed as `void*` / `const void*` holding IEEE binary16.
+ *
+ * All device pointers are owned by the caller.  All launches are
+ * asynchronous on `stream`.
+ *
+ * Alignment contract: Kq, Vq, K and V must be 16-byte aligned (cudaMalloc and
+ * torch allocations are 256-byte aligned).  Q, O, scale arrays and partials need only
+ * their natural alignment.
+ */
+#ifndef TQKV_H_
+#define TQKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tqkv_status {
+    TQKV_OK = 0,
+    /* D / block_size / lanes / tile outside the set the reference accepts */
+    TQKV_ERR_UNSUPPORTED = 1,
+    /* B, H or S negative or zero where the operation has no defined result,
+       or an element count that overflows */
+    TQKV_ERR_INVALID_SIZE = 2,
+    /* a pointer that must be 16-byte aligned is not */
+    TQKV_ERR_MISALIGNED = 3,
+    /* workspace pointer null or smaller than tqkv_decode_workspace_bytes() */
+    TQKV_ERR_WORKSPACE = 4,
+    /* a CUDA runtime call failed; tqkv_last_cuda_error() names it */
+    TQKV_ERR_CUDA = 5,
+    /* a required pointer is null */
+    TQKV_ERR_NULL = 6
+} tqkv_status;
+
+/* Human-readable name of a status. */
+const char* tqkv_status_string(tqkv_status s);
+
+/* The cudaError_t (as int) behind the most recent TQKV_ERR_CUDA on this host
+   thread, 0 if none. */
+int tqkv_last_cuda_error(void);
+
+/* Library version string, e.g. "tqkv-b200 0.1.0 sm_100a". */
+const char* tqkv_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Kernel A — blockwise symmetric FP16 -> INT8 compression.
+ *
+ * Replaces launch_kv_compress (reference include/quantization.h:15-20,
+ * src/kv_compress.cu:111-136).  Per token row and per block of `block_size`
+ * lanes along D: m = max|x|, s = m / 127 (s = 1 when m == 0), the fp16 scale
+ * is fp16(s) rounded to nearest-even, and each code is
+ * round-half-even(x / s) clamped to [-127, 127] — with the fp32 s, not the
+ * fp16 one (reference src/kv_compress.cu:81-95).  The divisions use the same
+ * fast-math division the reference is built with (CMakeLists.txt:21), so codes
+ * and scales are bit-identical to the reference build.
+ *
+ * Accepted: D in {64, 128}; block_size in {32, 64, 128}; block_size <= D.
+ */
+tqkv_status tqkv_kv_compress(const void* x, int8_t* xq, void* scales,
+                             int B, int H, int S, int D, int block_size,
+                             cudaStream_t stream);
+
+/* Kernel B — y = fp16(float(code) * float(scale)).
+ * Replaces launch_kv_reconstruct (reference include/quantization.h:22-27,
+ * src/kv_reconstruct.cu:10-34).  Same accepted set as tqkv_kv_compress. */
+tqkv_status tqkv_kv_reconstruct(const int8_t* xq, const void* scales, void* y,
+                                int B, int H, int S, int D, int block_size,
+                                cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Decode attention: O[b,h,:] = softmax(q . K^T / sqrt(D)) . V per (b, h).
+ *
+ * The work of all B*H heads is cut into equal runs of token rows, one run per
+ * CTA; a head that spans several CTAs is merged by the last CTA to finish it
+ * (log-sum-exp), using `workspace`.  Size the workspace with
+ * tqkv_decode_workspace_bytes() and zero it once with tqkv_workspace_init()
+ * before its first use; every decode call leaves it zeroed again.  Calls that
+ * share one workspace must be ordered (same stream, or events).
+ */
+size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D);
+
+tqkv_status tqkv_workspace_init(void* workspace, size_t workspace_bytes,
+                                cudaStream_t stream);
+
+/* Kernel D — fused INT8 decode with single-pass online softmax.
+ * Replaces launch_decode_attn_int8_fused_online (reference
+ * include/attention.h:28-35, src/attention_int8_fused_online.cu:16-239) and
+ * launch_decode_attn_int8_fused (attention.h:17-23,
+ * src/attention_int8_fused.cu:18-191): both compute the same function.
+ * Accepted: D in {64, 128}; block_size in {32, 64, 128}; block_size <= D.
+ * S == 0 writes NaN to O (what the reference online kernel yields). */
+tqkv_status tqkv_decode_int8(const void* q,
+                             const int8_t* kq, const void* ks,
+                             const int8_t* vq, const void* vs,
+                             void* o,
+                             int B, int H, int S, int D, int block_size,
+                             void* workspace, size_t workspace_bytes,
+                             cudaStream_t stream);
+
+/* FP16 decode attention on the same split-S skeleton.
+ * Replaces launch_decode_attn_baseline (reference include/attention.h:6-12,
+ * src/attention_baseline.cu:11-155) without its S <= ~12k shared-memory cap.
+ * Accepted: D in {64, 128}.  S == 0 writes 0 to O (as the reference). */
+tqkv_status tqkv_decode_fp16(const void* q, const void* k, const void* v,
+                             void* o, int B, int H, int S, int D,
+                             void* workspace, size_t workspace_bytes,
+                             cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Split-S decode across devices (no counterpart in the reference, which has
+ * no multi-GPU path).  Each device holds a slice [s0, s0 + S) of the tokens
+ * of every head and calls tqkv_decode_int8_partial on it; the partial record
+ * of head i is `partial + i * (D + 2)` floats laid out as
+ *     acc[0..D-1]  = sum_t exp(s_t - m) * v_t      (un-normalised)
+ *     acc[D]       = m = max_t s_t                  (natural-log units)
+ *     acc[D + 1]   = l = sum_t exp(s_t - m)
+ * with s_t = q . k_t / sqrt(D).  The records of R devices, gathered into
+ * [R][B*H][D + 2], are merged by tqkv_lse_combine into O.  S may be 0 for a
+ * device that holds no tokens (its record is m = -inf, l = 0, acc = 0). */
+tqkv_status tqkv_decode_int8_partial(const void* q,
+                                     const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs,
+                                     float* partial,
+                                     int B, int H, int S, int D, int block_size,
+                                     void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream);
+
+tqkv_status tqkv_lse_combine(const float* partials, void* o,
+                             int R, int BH, int D, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Device-side failure flag.  Every wait inside the kernels is bounded; a wait
+ * that runs out records a nonzero code here (and the kernel returns early)
+ * instead of hanging the GPU.  Reads and clears the flag of the current
+ * device (synchronous). */
+tqkv_status tqkv_read_device_error(uint32_t* code_out);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* TQKV_H_ */

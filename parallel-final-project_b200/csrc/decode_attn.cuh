@@ -1,0 +1,758 @@
+// decode_attn.cuh — split-S single-token decode attention for sm_100a.
+//
+// One kernel serves Kernel D (INT8 KV, fused online softmax; reference
+// src/attention_int8_fused_online.cu:16-176), Kernel C (same function,
+// reference src/attention_int8_fused.cu:18-143) and the FP16 baseline
+// (reference src/attention_baseline.cu:11-129):
+//
+//   O[bh, :] = sum_t softmax_t(q . k_t / sqrt(D)) * v_t
+//
+// with k_t = code_t * scale_t(block) for INT8 KV (dequantised in registers,
+// never written back).
+//
+// Work split ("flat split-S").  The B*H*S token rows are cut into equal runs
+// of R rows, one run per CTA (R = ceil(B*H*S / grid)), so every CTA streams the
+// same number of bytes whatever B, H and S are.  A run covers the tail of one
+// head, whole heads, and the head of another; each piece ("segment") yields an
+// online-softmax state (m, l, acc[D]).  A head that lies inside one run is
+// finished by that CTA; a head cut across CTAs writes one partial per CTA to
+// the workspace and the last CTA to arrive (atomic ticket) merges them by
+// log-sum-exp and writes O.  The ticket is reset by that CTA, so the
+// workspace stays zeroed between calls.
+//
+// CTA = 4 consumer warps + 1 producer warp.  One producer lane streams tiles
+// of TILE tokens (K rows, V rows, their fp16 scales, and q at the start of a
+// segment) from HBM into a ring of STAGES shared-memory buffers with 1-D bulk
+// async copies (cp.async.bulk, mbarrier completion, L2 evict-first; no
+// multicast).  Consumers never touch global memory on the hot loop.
+//
+// Consumer mapping.  A token row is split over LPR lanes, 16 bytes each
+// (LPR = 8 for D = 128 INT8).  The LPR lanes of a "lane group" own 4 rows of
+// every tile (rows g, g + G, g + 2G, g + 3G for G groups, so a warp's 16-byte
+// shared loads cover consecutive rows without bank conflicts) and keep their
+// own online-softmax state; the 16 (32) group states are merged once per
+// segment, with shuffles inside a warp and shared memory across warps.
+//
+// INT8 dot products.  q is turned once per segment into a 16-bit fixed-point
+// vector with a power-of-two scale (exact for every element within 2^4 of
+// max|q|; absolute error <= max|q| * 2^-15 otherwise) split into a signed
+// high byte and an unsigned low byte, so q . code is an exact integer built
+// from 8 dp4a per lane per token — no int8 -> float conversion on the K side.
+// The score is that integer times (scale_t * 2^-shift / sqrt(D) * log2 e).
+// V codes are converted with the exponent trick
+// (float bits 0x4B000000 | (byte ^ 0x80)) - (2^23 + 128), exact, one byte
+// permute and one add per element, then accumulated with FMA in fp32.
+// Softmax runs in base 2 with ex2.approx (the reference uses __expf).
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+#include "device_common.cuh"
+
+namespace tqkv {
+
+constexpr int kDecodeConsumerWarps = 4;
+constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
+constexpr int kDecodeThreads = kDecodeConsumers + 32;
+constexpr int kDecodeTileBytes = 8192;  // bytes of K (and of V) per stage
+constexpr int kDecodeStages = 4;
+constexpr int kMergeBarrier = 1;        // named barrier id used by consumers
+
+enum DecodeOut : int {
+    kOutHalf = 0,     // write O (fp16)
+    kOutPartial = 1,  // write per-head (acc[D], m, l) records, natural-log units
+};
+
+struct DecodeArgs {
+    const void* q;             // fp16 [BH][D]
+    const void* k;             // int8 or fp16 [BH][S][D]
+    const void* v;
+    const uint16_t* ks;        // fp16 [BH][S][D/BS] (INT8 only)
+    const uint16_t* vs;
+    void* out;                 // fp16 O [BH][D] or float [BH][D+2]
+    float* parts;              // workspace [BH][max_parts][D+2] (log2 units)
+    unsigned int* tickets;     // workspace [BH]
+    long long total_rows;      // BH * S
+    long long rows_per_cta;    // R
+    int S;
+    int BH;
+    int max_parts;
+    float score_scale_log2;    // log2(e) / sqrt(D)
+};
+
+template <int D, int BS, bool kHalfKV>
+struct DecodeCfg {
+    static constexpr int kElem = kHalfKV ? 2 : 1;
+    static constexpr int kRowBytes = D * kElem;
+    static constexpr int kLPR = kRowBytes / 16;                 // lanes per token row
+    static constexpr int kGroups = kDecodeConsumers / kLPR;     // lane groups per CTA
+    static constexpr int kTile = kDecodeTileBytes / kRowBytes;  // tokens per stage
+    static constexpr int kTPG = kTile / kGroups;                // tokens per group per stage
+    static constexpr int kEPL = 16 / kElem;                     // elements per lane
+    static constexpr int kNSub = kHalfKV ? 1 : D / BS;          // scales per row
+    static constexpr int kScaleBytes = kHalfKV ? 0 : kTile * kNSub * 2;
+    static constexpr int kScaleSlot = kHalfKV ? 0 : kScaleBytes + 32;  // + alignment slack
+    static constexpr int kQSlot = D * 2 + 32;
+    // stage layout (all offsets multiples of 16)
+    static constexpr int kOffK = 0;
+    static constexpr int kOffV = kDecodeTileBytes;
+    static constexpr int kOffKS = 2 * kDecodeTileBytes;
+    static constexpr int kOffVS = kOffKS + kScaleSlot;
+    static constexpr int kOffQ = kOffVS + kScaleSlot;
+    static constexpr int kStageBytes = kOffQ + kQSlot;
+    // merge scratch after the ring
+    static constexpr int kOffMerge = kDecodeStages * kStageBytes;
+    static constexpr int kMergeBytes = kDecodeConsumerWarps * (D + 2) * 4;
+    static constexpr int kOffBars = kOffMerge + kMergeBytes;
+    static constexpr int kSmemBytes = kOffBars + 2 * kDecodeStages * 8 + 16;
+
+    static_assert(kTPG == 4, "each lane group owns 4 rows per stage");
+    static_assert(kStageBytes % 16 == 0, "stage must stay 16-byte aligned");
+    static_assert(kOffMerge % 16 == 0 && kOffBars % 8 == 0, "alignment");
+};
+
+// Bytes [src, src + n) (src even, n even) of the buffer [lo, hi) land in
+// shared memory at dst + (src & 15).  The 16-byte-aligned part that lies
+// inside the buffer goes by bulk copy (returned: its byte count, to be added
+// to the stage's expected transaction count); the at most two ragged ends at
+// the buffer's own edges are copied with plain 2-byte loads.  Never reads
+// outside [lo, hi).
+struct Span {
+    uint64_t bulk_src;
+    uint32_t bulk_dst_off;
+    uint32_t bulk_bytes;
+};
+
+__device__ __forceinline__ Span plan_span(uint64_t src, uint32_t n, uint64_t lo, uint64_t hi) {
+    const uint64_t a16 = src & ~uint64_t(15);
+    const uint64_t b16 = (src + n + 15) & ~uint64_t(15);
+    const uint64_t lo16 = (lo + 15) & ~uint64_t(15);
+    const uint64_t hi16 = hi & ~uint64_t(15);
+    const uint64_t blo = a16 > lo16 ? a16 : lo16;
+    const uint64_t bhi = b16 < hi16 ? b16 : hi16;
+    Span s;
+    if (blo < bhi) {
+        s.bulk_src = blo;
+        s.bulk_dst_off = static_cast<uint32_t>(blo - a16);
+        s.bulk_bytes = static_cast<uint32_t>(bhi - blo);
+    } else {
+        s.bulk_src = 0;
+        s.bulk_dst_off = 0;
+        s.bulk_bytes = 0;
+    }
+    return s;
+}
+
+// Plain-load the parts of [src, src + n) not covered by the bulk span.
+__device__ __forceinline__ void copy_span_edges(uint8_t* dst, uint64_t src, uint32_t n,
+                                                const Span& s) {
+    const uint64_t a16 = src & ~uint64_t(15);
+    const uint64_t end = src + n;
+    const uint64_t cov_lo = s.bulk_bytes ? s.bulk_src : end;
+    const uint64_t cov_hi = s.bulk_bytes ? s.bulk_src + s.bulk_bytes : end;
+#pragma unroll 1
+    for (uint64_t p = src; p < end; p += 2) {
+        if (p >= cov_lo && p < cov_hi) {
+            p = cov_hi - 2;  // skip the bulk-covered range
+            continue;
+        }
+        const uint16_t v = __ldg(reinterpret_cast<const unsigned short*>(p));
+        *reinterpret_cast<uint16_t*>(dst + (p - a16)) = v;
+    }
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Producer: one lane streams every tile of this CTA's run into the ring.
+template <int D, int BS, bool kHalfKV>
+__device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* smem,
+                                                uint64_t* full, uint64_t* empty,
+                                                long long r0, long long r1) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    const uint64_t policy = make_evict_first_policy();
+    const uint64_t q_lo = reinterpret_cast<uint64_t>(a.q);
+    const uint64_t q_hi = q_lo + static_cast<uint64_t>(a.BH) * D * 2;
+    const uint64_t ks_lo = reinterpret_cast<uint64_t>(a.ks);
+    const uint64_t vs_lo = reinterpret_cast<uint64_t>(a.vs);
+    const uint64_t sc_bytes = static_cast<uint64_t>(a.total_rows) * C::kNSub * 2;
+    const uint8_t* kbase = static_cast<const uint8_t*>(a.k);
+    const uint8_t* vbase = static_cast<const uint8_t*>(a.v);
+
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (long long r = r0; r < r1 && ok;) {
+        const int bh = static_cast<int>(r / a.S);
+        const long long head0 = static_cast<long long>(bh) * a.S;
+        const int t_a = static_cast<int>(r - head0);
+        const int t_b = static_cast<int>((r1 - head0) < a.S ? (r1 - head0) : a.S);
+        for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
+            const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+                record_device_error(kErrEmptyWaitTimeout);
+                ok = false;
+                break;
+            }
+            uint8_t* st = smem + stage * C::kStageBytes;
+            const long long row0 = head0 + t0;
+            const uint32_t kv_bytes = static_cast<uint32_t>(cnt) * C::kRowBytes;
+            uint32_t tx = 2 * kv_bytes;
+
+            Span sk{}, sv{}, sq{};
+            uint64_t ks_src = 0, vs_src = 0, q_src = 0;
+            uint32_t sc_n = 0;
+            if constexpr (!kHalfKV) {
+                sc_n = static_cast<uint32_t>(cnt) * C::kNSub * 2;
+                ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                sk = plan_span(ks_src, sc_n, ks_lo, ks_lo + sc_bytes);
+                sv = plan_span(vs_src, sc_n, vs_lo, vs_lo + sc_bytes);
+                tx += sk.bulk_bytes + sv.bulk_bytes;
+                copy_span_edges(st + C::kOffKS, ks_src, sc_n, sk);
+                copy_span_edges(st + C::kOffVS, vs_src, sc_n, sv);
+            }
+            const bool first = (t0 == t_a);
+            if (first) {
+                q_src = q_lo + static_cast<uint64_t>(bh) * D * 2;
+                sq = plan_span(q_src, D * 2, q_lo, q_hi);
+                tx += sq.bulk_bytes;
+                copy_span_edges(st + C::kOffQ, q_src, D * 2, sq);
+            }
+            mbar_arrive_expect_tx(&full[stage], tx);
+            bulk_copy_g2s(st + C::kOffK, kbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
+                          policy);
+            bulk_copy_g2s(st + C::kOffV, vbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
+                          policy);
+            if constexpr (!kHalfKV) {
+                if (sk.bulk_bytes)
+                    bulk_copy_g2s(st + C::kOffKS + sk.bulk_dst_off,
+                                  reinterpret_cast<const void*>(sk.bulk_src), sk.bulk_bytes,
+                                  &full[stage], policy);
+                if (sv.bulk_bytes)
+                    bulk_copy_g2s(st + C::kOffVS + sv.bulk_dst_off,
+                                  reinterpret_cast<const void*>(sv.bulk_src), sv.bulk_bytes,
+                                  &full[stage], policy);
+            }
+            if (first && sq.bulk_bytes) {
+                bulk_copy_g2s(st + C::kOffQ + sq.bulk_dst_off,
+                              reinterpret_cast<const void*>(sq.bulk_src), sq.bulk_bytes,
+                              &full[stage], policy);
+            }
+            ++issued;
+            if (++stage == kDecodeStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        r = head0 + t_b;
+    }
+    // Drain: do not leave the CTA while copies into its shared memory are in
+    // flight.  In a normal run every stage was consumed long ago.
+    const int outstanding = issued < kDecodeStages ? static_cast<int>(issued) : kDecodeStages;
+    for (int i = 0; i < outstanding; ++i) {
+        if (--stage < 0) {
+            stage = kDecodeStages - 1;
+            phase ^= 1u;
+        }
+        if (!mbar_wait_bounded(&full[stage], phase)) {
+            record_device_error(kErrDrainTimeout);
+            break;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Consumer-side per-segment state and tile processing.
+
+template <int D, int BS, bool kHalfKV>
+struct SegState {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    float m2;             // running max of base-2 scores
+    float l;              // running sum of 2^(s - m2)
+    float acc[C::kEPL];   // running sum of 2^(s - m2) * v over this lane's dims
+    // INT8: q as fixed point, high and low bytes, 4 dims per word
+    int qh[4];
+    uint32_t ql[4];
+    float cq;             // 2^-shift * log2(e) / sqrt(D)
+    // FP16: q in fp32
+    float qf[kHalfKV ? C::kEPL : 1];
+};
+
+template <int D, int BS, bool kHalfKV>
+__device__ __forceinline__ void load_q(SegState<D, BS, kHalfKV>& st, const uint8_t* qsm,
+                                       int r, float score_scale_log2) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    const bool aligned = (reinterpret_cast<uintptr_t>(qsm) & 15) == 0;
+    const uint16_t* qh16 = reinterpret_cast<const uint16_t*>(qsm) + r * C::kEPL;
+    float qv[C::kEPL];
+    if (aligned) {
+        uint32_t w[C::kEPL / 2];
+#pragma unroll
+        for (int i = 0; i < C::kEPL / 8; ++i) {
+            const uint4 v = *reinterpret_cast<const uint4*>(qh16 + 8 * i);
+            w[4 * i + 0] = v.x;
+            w[4 * i + 1] = v.y;
+            w[4 * i + 2] = v.z;
+            w[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < C::kEPL / 2; ++i) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+            qv[2 * i] = __low2float(h);
+            qv[2 * i + 1] = __high2float(h);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < C::kEPL; ++i) qv[i] = half_bits_to_float(qh16[i]);
+    }
+
+    if constexpr (kHalfKV) {
+#pragma unroll
+        for (int i = 0; i < C::kEPL; ++i) st.qf[i] = qv[i];
+        st.cq = score_scale_log2;
+    } else {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < C::kEPL; ++i) amax = fmaxf(amax, fabsf(qv[i]));
+#pragma unroll
+        for (int off = 1; off < C::kLPR; off <<= 1)
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        // shift so that max|q| * 2^shift lies in [2^14, 2^15): |Qi| <= 32752
+        const int e = amax > 0.0f ? ((__float_as_int(amax) >> 23) & 0xff) - 127 : 0;
+        const int shift = 14 - e;
+        const float mul = __int_as_float((shift + 127) << 23);
+        const float inv = __int_as_float((127 - shift) << 23);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            uint32_t hi = 0, lo = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int qi = __float2int_rn(qv[4 * w + b] * mul);
+                hi |= (static_cast<uint32_t>(qi >> 8) & 0xffu) << (8 * b);
+                lo |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * b);
+            }
+            st.qh[w] = static_cast<int>(hi);
+            st.ql[w] = lo;
+        }
+        st.cq = inv * score_scale_log2;
+    }
+    st.m2 = -INFINITY;
+    st.l = 0.0f;
+#pragma unroll
+    for (int i = 0; i < C::kEPL; ++i) st.acc[i] = 0.0f;
+}
+
+
+// Exact int8 -> fp32 of byte b of a word already XOR-ed with 0x80808080:
+// the float with bits 0x4B0000uu is 2^23 + uu, and uu = code + 128.
+template <int b>
+__device__ __forceinline__ float biased_byte_to_float(uint32_t u) {
+    return __int_as_float(static_cast<int>(__byte_perm(u, 0x4B000000u, 0x7440u + b))) -
+           8388736.0f;
+}
+
+// Shared-memory byte offset, inside a stage's scale slot, of the first scale
+// of a tile whose first row is `row0`: the producer places global byte
+// address A at slot + (A & 15).
+__device__ __forceinline__ int scale_slot_offset(const uint16_t* base, long long row0, int nsub) {
+    return static_cast<int>((reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(row0) * nsub * 2) & 15);
+}
+
+template <int D, int BS, bool kHalfKV>
+__device__ __forceinline__ void consume_tile(SegState<D, BS, kHalfKV>& st, const uint8_t* stage,
+                                             int cnt, int ks_off, int vs_off, int g, int r) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    constexpr int kTPG = C::kTPG;
+    int rows[kTPG];
+#pragma unroll
+    for (int j = 0; j < kTPG; ++j) rows[j] = g + C::kGroups * j;
+
+    // ---- scores, base 2 ----
+    float s[kTPG];
+    if constexpr (!kHalfKV) {
+        const uint8_t* ksm = stage + C::kOffKS + ks_off;
+        const int blk = (16 * r) / BS;
+        int dot[kTPG];
+#pragma unroll
+        for (int j = 0; j < kTPG; ++j) {
+            const uint4 kw = lds128(stage + C::kOffK + rows[j] * C::kRowBytes + 16 * r);
+            int h = dp4a_ss(static_cast<int>(kw.x), st.qh[0], 0);
+            h = dp4a_ss(static_cast<int>(kw.y), st.qh[1], h);
+            h = dp4a_ss(static_cast<int>(kw.z), st.qh[2], h);
+            h = dp4a_ss(static_cast<int>(kw.w), st.qh[3], h);
+            int t = dp4a_us(st.ql[0], static_cast<int>(kw.x), h << 8);
+            t = dp4a_us(st.ql[1], static_cast<int>(kw.y), t);
+            t = dp4a_us(st.ql[2], static_cast<int>(kw.z), t);
+            t = dp4a_us(st.ql[3], static_cast<int>(kw.w), t);
+            dot[j] = t;
+        }
+        if constexpr (C::kNSub == 1) {
+            // one scale per row: reduce the exact integers, then scale once
+#pragma unroll
+            for (int off = 1; off < C::kLPR; off <<= 1) {
+#pragma unroll
+                for (int j = 0; j < kTPG; ++j) dot[j] += __shfl_xor_sync(0xffffffffu, dot[j], off);
+            }
+#pragma unroll
+            for (int j = 0; j < kTPG; ++j) {
+                const float ks = half_bits_to_float(
+                    *reinterpret_cast<const uint16_t*>(ksm + 2 * rows[j]));
+                s[j] = static_cast<float>(dot[j]) * (ks * st.cq);
+            }
+        } else {
+            // several blocks per row: scale each lane's block partial, then reduce
+#pragma unroll
+            for (int j = 0; j < kTPG; ++j) {
+                const float ks = half_bits_to_float(*reinterpret_cast<const uint16_t*>(
+                    ksm + 2 * (rows[j] * C::kNSub + blk)));
+                s[j] = static_cast<float>(dot[j]) * ks;
+            }
+#pragma unroll
+            for (int off = 1; off < C::kLPR; off <<= 1) {
+#pragma unroll
+                for (int j = 0; j < kTPG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
+            }
+#pragma unroll
+            for (int j = 0; j < kTPG; ++j) s[j] *= st.cq;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kTPG; ++j) {
+            const uint4 kw = lds128(stage + C::kOffK + rows[j] * C::kRowBytes + 16 * r);
+            const uint32_t w[4] = {kw.x, kw.y, kw.z, kw.w};
+            float d = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                d = fmaf(st.qf[2 * i], kf.x, d);
+                d = fmaf(st.qf[2 * i + 1], kf.y, d);
+            }
+            s[j] = d;
+        }
+#pragma unroll
+        for (int off = 1; off < C::kLPR; off <<= 1) {
+#pragma unroll
+            for (int j = 0; j < kTPG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
+        }
+#pragma unroll
+        for (int j = 0; j < kTPG; ++j) s[j] *= st.cq;
+    }
+#pragma unroll
+    for (int j = 0; j < kTPG; ++j) s[j] = rows[j] < cnt ? s[j] : -INFINITY;
+
+    // ---- online softmax update (base 2) ----
+    float mt = s[0];
+#pragma unroll
+    for (int j = 1; j < kTPG; ++j) mt = fmaxf(mt, s[j]);
+    const float m_new = fmaxf(st.m2, mt);
+    const float base = m_new == -INFINITY ? 0.0f : m_new;  // nothing seen yet: all terms 0
+    const float alpha = fast_exp2(st.m2 - base);
+    float e[kTPG];
+    float esum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kTPG; ++j) {
+        e[j] = fast_exp2(s[j] - base);
+        esum += e[j];
+    }
+    st.l = st.l * alpha + esum;
+    st.m2 = m_new;
+#pragma unroll
+    for (int i = 0; i < C::kEPL; ++i) st.acc[i] *= alpha;
+
+    // ---- weighted V ----
+    if constexpr (!kHalfKV) {
+        const uint8_t* vsm = stage + C::kOffVS + vs_off;
+        const int blk = (16 * r) / BS;
+#pragma unroll
+        for (int j = 0; j < kTPG; ++j) {
+            const float vsc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(
+                vsm + 2 * (rows[j] * C::kNSub + blk)));
+            // rows past cnt hold stale bytes (finite codes) and maybe a stale
+            // scale; their weight is forced to exactly 0.
+            const float w = rows[j] < cnt ? e[j] * vsc : 0.0f;
+            const uint4 vw = lds128(stage + C::kOffV + rows[j] * C::kRowBytes + 16 * r);
+            const uint32_t u[4] = {vw.x ^ 0x80808080u, vw.y ^ 0x80808080u, vw.z ^ 0x80808080u,
+                                   vw.w ^ 0x80808080u};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                st.acc[4 * i + 0] = fmaf(w, biased_byte_to_float<0>(u[i]), st.acc[4 * i + 0]);
+                st.acc[4 * i + 1] = fmaf(w, biased_byte_to_float<1>(u[i]), st.acc[4 * i + 1]);
+                st.acc[4 * i + 2] = fmaf(w, biased_byte_to_float<2>(u[i]), st.acc[4 * i + 2]);
+                st.acc[4 * i + 3] = fmaf(w, biased_byte_to_float<3>(u[i]), st.acc[4 * i + 3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kTPG; ++j) {
+            if (rows[j] < cnt) {  // stale fp16 rows may hold Inf/NaN: skip, do not weight by 0
+                const uint4 vw = lds128(stage + C::kOffV + rows[j] * C::kRowBytes + 16 * r);
+                const uint32_t w4[4] = {vw.x, vw.y, vw.z, vw.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+                    st.acc[2 * i] = fmaf(e[j], vf.x, st.acc[2 * i]);
+                    st.acc[2 * i + 1] = fmaf(e[j], vf.y, st.acc[2 * i + 1]);
+                }
+            }
+        }
+    }
+}
+
+// Merge two base-2 online-softmax states: (m, l, acc) <- (m, l, acc) (+) (mo, lo, acco).
+__device__ __forceinline__ void lse_factors(float m, float mo, float& M, float& fa, float& fb) {
+    M = fmaxf(m, mo);
+    const float base = M == -INFINITY ? 0.0f : M;
+    fa = fast_exp2(m - base);
+    fb = fast_exp2(mo - base);
+}
+
+// Finish one segment: merge the lane-group states of the CTA, then either
+// write O / the partial record (head owned by this CTA alone), or publish a
+// partial and let the last CTA of the head merge all of them.
+template <int D, int BS, bool kHalfKV, int OUT>
+__device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, const DecodeArgs& a,
+                                               float* merge, int* flag, int bh, int part,
+                                               int nparts, int tid) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    // 1) lane groups inside a warp: lanes l, l + LPR, ... hold the same dims
+#pragma unroll
+    for (int off = C::kLPR; off < 32; off <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, st.m2, off);
+        const float lo = __shfl_xor_sync(0xffffffffu, st.l, off);
+        float M, fa, fb;
+        lse_factors(st.m2, mo, M, fa, fb);
+        st.l = st.l * fa + lo * fb;
+#pragma unroll
+        for (int i = 0; i < C::kEPL; ++i) {
+            const float ao = __shfl_xor_sync(0xffffffffu, st.acc[i], off);
+            st.acc[i] = st.acc[i] * fa + ao * fb;
+        }
+        st.m2 = M;
+    }
+    // 2) warps, through shared memory: merge[w][0..D-1] = acc, [D] = m2, [D+1] = l
+    float* mw = merge + warp * (D + 2);
+    if (lane < C::kLPR) {
+#pragma unroll
+        for (int i = 0; i < C::kEPL; ++i) mw[lane * C::kEPL + i] = st.acc[i];
+        if (lane == 0) {
+            mw[D] = st.m2;
+            mw[D + 1] = st.l;
+        }
+    }
+    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+
+    float A = 0.0f, M = -INFINITY, L = 0.0f;
+    if (tid < D) {
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) M = fmaxf(M, merge[w * (D + 2) + D]);
+        const float base = M == -INFINITY ? 0.0f : M;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+            const float f = fast_exp2(merge[w * (D + 2) + D] - base);
+            L = fmaf(merge[w * (D + 2) + D + 1], f, L);
+            A = fmaf(merge[w * (D + 2) + tid], f, A);
+        }
+    }
+
+    constexpr float kLn2 = 0.69314718055994530942f;
+    if (nparts == 1) {
+        if (tid < D) {
+            if constexpr (OUT == kOutHalf) {
+                static_cast<__half*>(a.out)[static_cast<long long>(bh) * D + tid] =
+                    __float2half_rn(A * (1.0f / L));
+            } else {
+                float* rec = static_cast<float*>(a.out) + static_cast<long long>(bh) * (D + 2);
+                rec[tid] = A;
+                if (tid == 0) {
+                    rec[D] = M * kLn2;
+                    rec[D + 1] = L;
+                }
+            }
+        }
+        named_barrier_sync(kMergeBarrier, kDecodeConsumers);  // merge[] reused next segment
+        return;
+    }
+
+    // publish this CTA's piece of the head
+    float* mine = a.parts + (static_cast<long long>(bh) * a.max_parts + part) * (D + 2);
+    if (tid < D) {
+        mine[tid] = A;
+        if (tid == 0) {
+            mine[D] = M;
+            mine[D + 1] = L;
+        }
+    }
+    __threadfence();
+    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+    if (tid == 0) {
+        const unsigned int prev = atomicAdd(&a.tickets[bh], 1u);
+        *flag = (prev == static_cast<unsigned int>(nparts - 1)) ? 1 : 0;
+    }
+    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+    if (*flag) {
+        __threadfence();
+        const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
+        if (tid < D) {
+            float Mt = -INFINITY;
+            for (int p = 0; p < nparts; ++p) Mt = fmaxf(Mt, __ldcg(recs + p * (D + 2) + D));
+            const float base = Mt == -INFINITY ? 0.0f : Mt;
+            float At = 0.0f, Lt = 0.0f;
+            for (int p = 0; p < nparts; ++p) {
+                const float f = fast_exp2(__ldcg(recs + p * (D + 2) + D) - base);
+                Lt = fmaf(__ldcg(recs + p * (D + 2) + D + 1), f, Lt);
+                At = fmaf(__ldcg(recs + p * (D + 2) + tid), f, At);
+            }
+            if constexpr (OUT == kOutHalf) {
+                static_cast<__half*>(a.out)[static_cast<long long>(bh) * D + tid] =
+                    __float2half_rn(At * (1.0f / Lt));
+            } else {
+                float* rec = static_cast<float*>(a.out) + static_cast<long long>(bh) * (D + 2);
+                rec[tid] = At;
+                if (tid == 0) {
+                    rec[D] = Mt * kLn2;
+                    rec[D + 1] = Lt;
+                }
+            }
+        }
+        if (tid == 0) a.tickets[bh] = 0u;  // leave the workspace zeroed for the next call
+    }
+    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+}
+
+// ---------------------------------------------------------------------------
+template <int D, int BS, bool kHalfKV, int OUT>
+__global__ void __launch_bounds__(kDecodeThreads)
+    decode_attn_kernel(const DecodeArgs a) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+    uint64_t* empty = full + kDecodeStages;
+    int* flag = reinterpret_cast<int*>(empty + kDecodeStages);
+    float* merge = reinterpret_cast<float*>(smem + C::kOffMerge);
+
+    const long long r0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
+    const long long r1_raw = r0 + a.rows_per_cta;
+    const long long r1 = r1_raw < a.total_rows ? r1_raw : a.total_rows;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecodeStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kDecodeConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (r0 >= r1) return;
+
+    const int warp = threadIdx.x >> 5;
+    if (warp == kDecodeConsumerWarps) {
+        if ((threadIdx.x & 31) == 0) decode_producer<D, BS, kHalfKV>(a, smem, full, empty, r0, r1);
+        return;
+    }
+
+    const int tid = threadIdx.x;
+    const int g = tid / C::kLPR;
+    const int r = tid % C::kLPR;
+    const int lane = tid & 31;
+    int stage = 0;
+    uint32_t phase = 0;
+    SegState<D, BS, kHalfKV> st;
+    // A warp whose bounded wait ran out stops computing but keeps walking the
+    // schedule, so that the consumer-wide named barriers still see every warp.
+    bool broken = false;
+
+    for (long long rr = r0; rr < r1;) {
+        const int bh = static_cast<int>(rr / a.S);
+        const long long head0 = static_cast<long long>(bh) * a.S;
+        const int t_a = static_cast<int>(rr - head0);
+        const int t_b = static_cast<int>((r1 - head0) < a.S ? (r1 - head0) : a.S);
+        for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
+            const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
+            if (!broken) {
+                const bool ok = mbar_wait_bounded(&full[stage], phase);
+                broken = __any_sync(0xffffffffu, !ok);
+                if (broken && lane == 0) record_device_error(kErrFullWaitTimeout);
+            }
+            const uint8_t* sp = smem + stage * C::kStageBytes;
+            if (!broken) {
+                if (t0 == t_a) {
+                    const int q_off = static_cast<int>(
+                        (reinterpret_cast<uint64_t>(a.q) + static_cast<uint64_t>(bh) * D * 2) &
+                        15);
+                    load_q<D, BS, kHalfKV>(st, sp + C::kOffQ + q_off, r, a.score_scale_log2);
+                }
+                int ks_off = 0, vs_off = 0;
+                if constexpr (!kHalfKV) {
+                    ks_off = scale_slot_offset(a.ks, head0 + t0, C::kNSub);
+                    vs_off = scale_slot_offset(a.vs, head0 + t0, C::kNSub);
+                }
+                consume_tile<D, BS, kHalfKV>(st, sp, cnt, ks_off, vs_off, g, r);
+            } else if (t0 == t_a) {
+                st.m2 = -INFINITY;
+                st.l = 0.0f;
+#pragma unroll
+                for (int i = 0; i < C::kEPL; ++i) st.acc[i] = 0.0f;
+            }
+            __syncwarp();
+            if (lane == 0 && !broken) mbar_arrive(&empty[stage]);
+            if (++stage == kDecodeStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        // which CTAs hold pieces of this head
+        const long long c_first = head0 / a.rows_per_cta;
+        const long long c_last = (head0 + a.S - 1) / a.rows_per_cta;
+        const int nparts = static_cast<int>(c_last - c_first + 1);
+        const int part = static_cast<int>(blockIdx.x - c_first);
+        finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, flag, bh, part, nparts, tid);
+        rr = head0 + t_b;
+    }
+}
+
+// Log-sum-exp merge of R partial records per head (natural-log units):
+// partials [R][BH][D + 2] -> O fp16 [BH][D].  One warp-group per head.
+template <int D>
+__global__ void __launch_bounds__(D)
+    lse_combine_kernel(const float* __restrict__ partials, __half* __restrict__ o, int R, int BH) {
+    const int bh = blockIdx.x;
+    const int t = threadIdx.x;
+    const long long stride = static_cast<long long>(BH) * (D + 2);
+    const float* rec = partials + static_cast<long long>(bh) * (D + 2);
+    float M = -INFINITY;
+    for (int r = 0; r < R; ++r) M = fmaxf(M, rec[r * stride + D]);
+    const float base = M == -INFINITY ? 0.0f : M;
+    float A = 0.0f, L = 0.0f;
+    for (int r = 0; r < R; ++r) {
+        const float f = __expf(rec[r * stride + D] - base);
+        L = fmaf(rec[r * stride + D + 1], f, L);
+        A = fmaf(rec[r * stride + t], f, A);
+    }
+    o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
+}
+
+// Fill `n` fp16 values with `bits` (used for S == 0 outputs).
+__global__ void fill_half_kernel(uint16_t* __restrict__ p, long long n, uint16_t bits) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        p[i] = bits;
+}
+
+// Empty partial records (m = -inf, l = 0, acc = 0) for a device with S == 0.
+__global__ void fill_empty_partials_kernel(float* __restrict__ p, long long heads, int D) {
+    const long long n = heads * (D + 2);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % (D + 2));
+        p[i] = c == D ? -INFINITY : 0.0f;
+    }
+}
+
+}  // namespace tqkv

@@ -1,0 +1,194 @@
+// kv_compress.cuh — Kernel A (blockwise FP16 -> INT8) and Kernel B
+// (INT8 -> FP16 reconstruct) device code for sm_100a.
+//
+// Quantisation rule (reference src/kv_compress.cu:41-95), per token row and
+// per block of BS lanes along D:
+//     m     = max |x|                      (fp32 of the fp16 inputs)
+//     s     = m / 127 ; s = 1 if s == 0    (fp32)
+//     scale = fp16(s), round-to-nearest-even
+//     code  = clamp(round_half_even(x / s), -127, 127)   (x / s with fp32 s)
+//
+// B200 layout: one lane owns 8 consecutive elements (one 16-byte load of
+// fp16, one 8-byte store of codes); D/8 lanes cover a token row, so a warp
+// handles 32/(D/8) rows per step and the block max is a shuffle reduction
+// over BS/8 lanes.  A grid-stride loop over row groups replaces the
+// reference's one-CTA-per-row launch (16.7 M CTAs at S = 131072), with two
+// row groups in flight per warp.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+#include "device_common.cuh"
+
+namespace tqkv {
+
+// How x / y is evaluated inside Kernel A.  The reference is compiled with
+// --use_fast_math, under which a plain '/' is not an IEEE division.  The two
+// can round differently only where the exact quotient 127*x/m is a
+// half-integer (the "tie class"); there the approximate forms below all agree
+// with the reference build and IEEE does not.  The library instantiates
+// kDivApproxFtz (tqkv_capi.cu); the others are kept for the parity probe.
+enum DivMode : int {
+    kDivIEEE = 0,        // correctly rounded (div.rn.f32)
+    kDivApprox = 1,      // div.approx.f32
+    kDivApproxFtz = 2,   // div.approx.ftz.f32
+    kDivFull = 3,        // div.full.f32
+    kDivFullFtz = 4,     // div.full.ftz.f32
+};
+
+template <int MODE>
+__device__ __forceinline__ float kv_div(float a, float b) {
+    float r;
+    if constexpr (MODE == kDivIEEE) {
+        r = __fdiv_rn(a, b);
+    } else if constexpr (MODE == kDivApprox) {
+        asm("div.approx.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    } else if constexpr (MODE == kDivApproxFtz) {
+        asm("div.approx.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    } else if constexpr (MODE == kDivFull) {
+        asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    } else {
+        asm("div.full.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    }
+    return r;
+}
+
+constexpr int kCompressThreads = 256;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream_v2(uint2* p, uint2 v) {
+    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+__device__ __forceinline__ void st_stream_v4(uint4* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Quantise the 8 fp16 values in `raw` (lane c of a row) and store codes and,
+// on the first lane of each block, the block's fp16 scale.
+template <int D, int BS, int MODE>
+__device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool valid, int c,
+                                              uint2* __restrict__ xq,
+                                              __half* __restrict__ scales) {
+    constexpr int kLPR = D / 8;   // lanes per row
+    constexpr int kLPB = BS / 8;  // lanes per block
+    constexpr int kNSub = D / BS;
+
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        f[2 * i] = __low2float(h);
+        f[2 * i + 1] = __high2float(h);
+    }
+    // max |x| with fmaxf semantics (a NaN operand is ignored unless both are NaN),
+    // which makes the result independent of the reduction order.
+    float a = fabsf(f[0]);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) a = fmaxf(a, fabsf(f[i]));
+#pragma unroll
+    for (int off = 1; off < kLPB; off <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+
+    float s = kv_div<MODE>(a, 127.0f);
+    if (s == 0.0f) s = 1.0f;
+
+    if (valid && (c % kLPB) == 0) {
+        scales[row * kNSub + c / kLPB] = __float2half_rn(s);
+    }
+
+    uint32_t packed[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            int qi = __float2int_rn(kv_div<MODE>(f[4 * h + b], s));
+            qi = qi > 127 ? 127 : qi;
+            qi = qi < -127 ? -127 : qi;
+            word |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * b);
+        }
+        packed[h] = word;
+    }
+    if (valid) {
+        st_stream_v2(xq + row * kLPR + c, make_uint2(packed[0], packed[1]));
+    }
+}
+
+// x: fp16 rows as uint4 (8 halves each), xq: codes as uint2 (8 bytes each).
+template <int D, int BS, int MODE>
+__global__ void __launch_bounds__(kCompressThreads)
+    kv_compress_kernel(const uint4* __restrict__ x, uint2* __restrict__ xq,
+                       __half* __restrict__ scales, long long rows) {
+    constexpr int kLPR = D / 8;
+    constexpr int kRPW = 32 / kLPR;  // rows per warp step
+    const int lane = threadIdx.x & 31;
+    const int c = lane % kLPR;
+    const int rsub = lane / kLPR;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+
+    for (long long r0 = warp * (2 * kRPW); r0 < rows; r0 += nwarps * (2 * kRPW)) {
+        const long long row_a = r0 + rsub;
+        const long long row_b = r0 + kRPW + rsub;
+        const bool va = row_a < rows;
+        const bool vb = row_b < rows;
+        uint4 raw_a = make_uint4(0, 0, 0, 0), raw_b = make_uint4(0, 0, 0, 0);
+        if (va) raw_a = ld_stream_v4(x + row_a * kLPR + c);
+        if (vb) raw_b = ld_stream_v4(x + row_b * kLPR + c);
+        compress_lane<D, BS, MODE>(raw_a, row_a, va, c, xq, scales);
+        compress_lane<D, BS, MODE>(raw_b, row_b, vb, c, xq, scales);
+    }
+}
+
+// Kernel B: y = fp16(float(code) * float(scale)).  The product of a 7-bit
+// code and an 11-bit scale is exact in fp32, so the only rounding is the
+// final fp16 conversion, as in the reference (src/kv_reconstruct.cu:33).
+// One lane owns 16 codes (one 16-byte load, two 16-byte stores).
+template <int D, int BS>
+__global__ void __launch_bounds__(kCompressThreads)
+    kv_reconstruct_kernel(const uint4* __restrict__ xq, const __half* __restrict__ scales,
+                          uint4* __restrict__ y, long long rows) {
+    constexpr int kLPR = D / 16;
+    constexpr int kRPW = 32 / kLPR;
+    constexpr int kNSub = D / BS;
+    const int lane = threadIdx.x & 31;
+    const int c = lane % kLPR;
+    const int rsub = lane / kLPR;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+
+    for (long long r0 = warp * kRPW; r0 < rows; r0 += nwarps * kRPW) {
+        const long long row = r0 + rsub;
+        if (row >= rows) continue;
+        const uint4 raw = ld_stream_v4(xq + row * kLPR + c);
+        const float s = __half2float(scales[row * kNSub + (16 * c) / BS]);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int lo = static_cast<int8_t>((w[i] >> (16 * p)) & 0xffu);
+                const int hi = static_cast<int8_t>((w[i] >> (16 * p + 8)) & 0xffu);
+                const __half2 h = __halves2half2(__float2half_rn(static_cast<float>(lo) * s),
+                                                 __float2half_rn(static_cast<float>(hi) * s));
+                out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        st_stream_v4(y + (row * kLPR + c) * 2, make_uint4(out[0], out[1], out[2], out[3]));
+        st_stream_v4(y + (row * kLPR + c) * 2 + 1, make_uint4(out[4], out[5], out[6], out[7]));
+    }
+}
+
+}  // namespace tqkv

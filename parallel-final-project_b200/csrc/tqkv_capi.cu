@@ -1,0 +1,492 @@
+// tqkv_capi.cu — kernel instantiations, launch planning, the per-stream
+// workspace cache and the extern "C" ABI declared in include/tqkv.h.
+//
+// Everything device-side lives in this one translation unit (no relocatable
+// device code), so the device error flag of device_common.cuh is this TU's.
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <utility>
+
+#include "decode_attn.cuh"
+#include "device_common.cuh"
+#include "kv_compress.cuh"
+#include "tqkv.h"
+#include "tqkv_internal.h"
+
+#ifndef TQKV_COMPRESS_DIV_MODE
+// Division form used by Kernel A.  The reference is built with
+// --use_fast_math (CMakeLists.txt:21), under which its '/' is an approximate
+// division; div.approx.ftz.f32 reproduces its codes and scales bit for bit
+// (measured on the B200 against the reference build: 0 differences over
+// 2.9e9 elements of the five configurations and 3.7e7 tie-rich elements,
+// while IEEE division differs on ~15% of the tie-class elements).
+#define TQKV_COMPRESS_DIV_MODE tqkv::kDivApproxFtz
+#endif
+
+namespace tqkv {
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipeline fill
+constexpr int kMaxCtasPerSmBound = 4;      // >= any decode kernel's occupancy (smem-bound)
+
+struct KernelKey {
+    const void* fn;
+    int device;
+    bool operator<(const KernelKey& o) const {
+        return fn < o.fn || (fn == o.fn && device < o.device);
+    }
+};
+
+std::mutex g_kernel_mu;
+std::map<KernelKey, int> g_occupancy;  // resident CTAs per SM, after smem opt-in
+std::map<int, int> g_sm_count;
+
+int sm_count(int device) {
+    std::lock_guard<std::mutex> lock(g_kernel_mu);
+    auto it = g_sm_count.find(device);
+    if (it != g_sm_count.end()) return it->second;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) n = 0;
+    g_sm_count[device] = n;
+    return n;
+}
+
+// Opts the kernel into its dynamic shared memory once per device and returns
+// how many of its CTAs fit on one SM (0 on failure).
+template <typename Fn>
+int prepare_kernel(Fn fn, int threads, int smem_bytes, int device) {
+    const KernelKey key{reinterpret_cast<const void*>(fn), device};
+    std::lock_guard<std::mutex> lock(g_kernel_mu);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end()) return it->second;
+    if (smem_bytes > 48 * 1024) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) !=
+            cudaSuccess)
+            return 0;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem_bytes) !=
+        cudaSuccess)
+        per_sm = 0;
+    g_occupancy[key] = per_sm;
+    return per_sm;
+}
+
+struct DecodePlan {
+    int grid;
+    long long rows_per_cta;
+    int max_parts;
+};
+
+// Equal runs of rows per CTA.  `max_ctas` caps the grid (resident CTAs).
+DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
+    DecodePlan p{};
+    long long g = (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta;
+    if (g > max_ctas) g = max_ctas;
+    if (g < 1) g = 1;
+    long long r = (total_rows + g - 1) / g;
+    r = (r + 15) / 16 * 16;  // keeps 16-token alignment of run starts when S allows it
+    p.rows_per_cta = r;
+    p.grid = static_cast<int>((total_rows + r - 1) / r);
+    p.max_parts = static_cast<int>((static_cast<long long>(S) - 1) / r + 2);
+    return p;
+}
+
+// The workspace layout is fixed by an upper bound on the grid so that its
+// size does not depend on which decode kernel runs.
+DecodePlan bound_plan(long long total_rows, int S, int device) {
+    const long long cap = static_cast<long long>(sm_count(device)) * kMaxCtasPerSmBound;
+    return make_plan(total_rows, S, cap > 0 ? cap : 1);
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+    size_t tickets_off, parts_off, total;
+};
+
+WsLayout ws_layout(long long BH, int max_parts, int D) {
+    WsLayout w{};
+    w.tickets_off = 0;
+    w.parts_off = align_up(static_cast<size_t>(BH) * sizeof(unsigned int), 256);
+    w.total = w.parts_off +
+              align_up(static_cast<size_t>(BH) * max_parts * (D + 2) * sizeof(float), 256);
+    return w;
+}
+
+__global__ void empty_grid_kernel() {}
+
+// Launch through cudaLaunchKernel so the launch status comes back as a return
+// value without clearing (or reading) the host thread's pending CUDA error:
+// a failed launch stays visible to the caller's next error query, as with
+// the reference's <<<...>>> launches.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args... args) {
+    static_assert(sizeof...(KArgs) == sizeof...(Args), "argument count");
+    std::tuple<KArgs...> vals(static_cast<KArgs>(args)...);
+    void* ptrs[sizeof...(KArgs) > 0 ? sizeof...(KArgs) : 1];
+    std::apply([&](auto&... v) {
+        int i = 0;
+        ((ptrs[i++] = static_cast<void*>(&v)), ...);
+    }, vals);
+    return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, block, ptrs, smem, stream);
+}
+
+template <int D, int BS>
+tqkv_status compress_impl(const void* x, int8_t* xq, void* scales, long long rows,
+                          cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e);
+    auto fn = kv_compress_kernel<D, BS, TQKV_COMPRESS_DIV_MODE>;
+    const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
+    const long long rows_per_block = 2LL * (kCompressThreads / 32) * (32 / (D / 8));
+    long long grid = (rows + rows_per_block - 1) / rows_per_block;
+    const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    return from_cuda(launch_kernel(fn, dim3(static_cast<unsigned>(grid)), dim3(kCompressThreads), 0,
+                                   stream, static_cast<const uint4*>(x),
+                                   reinterpret_cast<uint2*>(xq), static_cast<__half*>(scales),
+                                   rows));
+}
+
+template <int D, int BS>
+tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long long rows,
+                             cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e);
+    auto fn = kv_reconstruct_kernel<D, BS>;
+    const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
+    const long long rows_per_block = (kCompressThreads / 32) * (32 / (D / 16));
+    long long grid = (rows + rows_per_block - 1) / rows_per_block;
+    const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    return from_cuda(launch_kernel(fn, dim3(static_cast<unsigned>(grid)), dim3(kCompressThreads), 0,
+                                   stream, reinterpret_cast<const uint4*>(xq),
+                                   static_cast<const __half*>(scales), static_cast<uint4*>(y),
+                                   rows));
+}
+
+template <int D, int BS, bool kHalfKV, int OUT>
+tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void* workspace,
+                        size_t workspace_bytes, cudaStream_t stream) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e);
+    auto fn = decode_attn_kernel<D, BS, kHalfKV, OUT>;
+    const int per_sm = prepare_kernel(fn, kDecodeThreads, C::kSmemBytes, dev);
+    if (per_sm <= 0) return from_cuda(cudaErrorInvalidConfiguration);
+
+    const DecodePlan bound = bound_plan(total_rows, S, dev);
+    const WsLayout lay = ws_layout(BH, bound.max_parts, D);
+    const long long resident = static_cast<long long>(sm_count(dev)) * per_sm;
+    const DecodePlan plan = make_plan(total_rows, S, resident);
+    if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: per_sm <= bound
+    const bool needs_ws = plan.grid > 1;
+    if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
+
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.tickets = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.tickets_off) : nullptr;
+    a.parts = needs_ws ? reinterpret_cast<float*>(ws + lay.parts_off) : nullptr;
+    a.total_rows = total_rows;
+    a.rows_per_cta = plan.rows_per_cta;
+    a.S = S;
+    a.BH = BH;
+    a.max_parts = bound.max_parts;
+    a.score_scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
+    return from_cuda(launch_kernel(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
+                                   stream, a));
+}
+
+template <int D, int BS, bool kHalfKV>
+tqkv_status decode_out(OutKind out, const DecodeArgs& a, long long total, int S, int BH,
+                       void* ws, size_t wsb, cudaStream_t stream) {
+    if (out == OutKind::kHalfO)
+        return decode_impl<D, BS, kHalfKV, kOutHalf>(a, total, S, BH, ws, wsb, stream);
+    return decode_impl<D, BS, kHalfKV, kOutPartial>(a, total, S, BH, ws, wsb, stream);
+}
+
+template <int D>
+tqkv_status combine_impl(const float* partials, void* o, int R, int BH, cudaStream_t stream) {
+    return from_cuda(launch_kernel(lse_combine_kernel<D>, dim3(BH), dim3(D), 0, stream, partials,
+                                   static_cast<__half*>(o), R, BH));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+tqkv_status from_cuda(cudaError_t err) {
+    if (err == cudaSuccess) return TQKV_OK;
+    t_last_cuda_error = static_cast<int>(err);
+    return TQKV_ERR_CUDA;
+}
+
+bool is_supported_int8(int D, int block_size) {
+    if (D == 64) return block_size == 32 || block_size == 64;
+    if (D == 128) return block_size == 32 || block_size == 64 || block_size == 128;
+    return false;
+}
+
+tqkv_status launch_compress(const void* x, int8_t* xq, void* scales, long long rows, int D,
+                            int bs, cudaStream_t stream) {
+    if (D == 64 && bs == 32) return compress_impl<64, 32>(x, xq, scales, rows, stream);
+    if (D == 64 && bs == 64) return compress_impl<64, 64>(x, xq, scales, rows, stream);
+    if (D == 128 && bs == 32) return compress_impl<128, 32>(x, xq, scales, rows, stream);
+    if (D == 128 && bs == 64) return compress_impl<128, 64>(x, xq, scales, rows, stream);
+    if (D == 128 && bs == 128) return compress_impl<128, 128>(x, xq, scales, rows, stream);
+    return TQKV_ERR_UNSUPPORTED;
+}
+
+tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, long long rows,
+                               int D, int bs, cudaStream_t stream) {
+    if (D == 64 && bs == 32) return reconstruct_impl<64, 32>(xq, scales, y, rows, stream);
+    if (D == 64 && bs == 64) return reconstruct_impl<64, 64>(xq, scales, y, rows, stream);
+    if (D == 128 && bs == 32) return reconstruct_impl<128, 32>(xq, scales, y, rows, stream);
+    if (D == 128 && bs == 64) return reconstruct_impl<128, 64>(xq, scales, y, rows, stream);
+    if (D == 128 && bs == 128) return reconstruct_impl<128, 128>(xq, scales, y, rows, stream);
+    return TQKV_ERR_UNSUPPORTED;
+}
+
+tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
+                          const void* v, const void* vs, void* o, int BH, int S, int D, int bs,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.ks = static_cast<const uint16_t*>(ks);
+    a.vs = static_cast<const uint16_t*>(vs);
+    a.out = o;
+    const long long total = static_cast<long long>(BH) * S;
+    if (kv == KvKind::kHalf) {
+        if (D == 64) return decode_out<64, 64, true>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+        if (D == 128) return decode_out<128, 128, true>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+        return TQKV_ERR_UNSUPPORTED;
+    }
+    if (D == 64 && bs == 32) return decode_out<64, 32, false>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 64 && bs == 64) return decode_out<64, 64, false>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 32) return decode_out<128, 32, false>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 64) return decode_out<128, 64, false>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 128) return decode_out<128, 128, false>(out, a, total, S, BH, workspace, workspace_bytes, stream);
+    return TQKV_ERR_UNSUPPORTED;
+}
+
+tqkv_status launch_fill_half(void* o, long long n, uint16_t bits, cudaStream_t stream) {
+    if (n <= 0) return TQKV_OK;
+    long long grid = (n + 255) / 256;
+    if (grid > 1024) grid = 1024;
+    return from_cuda(launch_kernel(fill_half_kernel, dim3(static_cast<unsigned>(grid)), dim3(256),
+                                   0, stream, static_cast<uint16_t*>(o), n, bits));
+}
+
+tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t stream) {
+    const long long n = heads * (D + 2);
+    if (n <= 0) return TQKV_OK;
+    long long grid = (n + 255) / 256;
+    if (grid > 1024) grid = 1024;
+    return from_cuda(launch_kernel(fill_empty_partials_kernel, dim3(static_cast<unsigned>(grid)),
+                                   dim3(256), 0, stream, p, heads, D));
+}
+
+size_t decode_workspace_bytes(long long BH, int S, int D) {
+    if (BH <= 0 || S <= 0) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const DecodePlan bound = bound_plan(BH * S, S, dev);
+    return ws_layout(BH, bound.max_parts, D).total;
+}
+
+namespace {
+struct CachedWs {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, CachedWs> g_ws;
+}  // namespace
+
+void* cached_workspace(cudaStream_t stream, size_t bytes, tqkv_status* status) {
+    *status = TQKV_OK;
+    if (bytes == 0) return nullptr;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *status = from_cuda(e);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    CachedWs& c = g_ws[{dev, stream}];
+    if (c.bytes >= bytes) return c.ptr;
+    if (c.ptr) {
+        // the old buffer may still be in use by work queued on this stream
+        e = cudaStreamSynchronize(stream);
+        if (e == cudaSuccess) e = cudaFree(c.ptr);
+        c.ptr = nullptr;
+        c.bytes = 0;
+        if (e != cudaSuccess) {
+            *status = from_cuda(e);
+            return nullptr;
+        }
+    }
+    void* p = nullptr;
+    e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, bytes, stream);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        *status = from_cuda(e);
+        return nullptr;
+    }
+    c.ptr = p;
+    c.bytes = bytes;
+    return p;
+}
+
+void raise_empty_grid_error(cudaStream_t stream) {
+    (void)launch_kernel(empty_grid_kernel, dim3(0), dim3(1), 0, stream);
+}
+
+}  // namespace tqkv
+
+// ===========================================================================
+// extern "C" ABI
+// ===========================================================================
+using tqkv::KvKind;
+using tqkv::OutKind;
+
+extern "C" {
+
+const char* tqkv_status_string(tqkv_status s) {
+    switch (s) {
+        case TQKV_OK: return "ok";
+        case TQKV_ERR_UNSUPPORTED: return "unsupported D / block_size / lanes / tile";
+        case TQKV_ERR_INVALID_SIZE: return "invalid size";
+        case TQKV_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+        case TQKV_ERR_WORKSPACE: return "workspace missing or too small";
+        case TQKV_ERR_CUDA: return "CUDA runtime error";
+        case TQKV_ERR_NULL: return "null pointer";
+    }
+    return "unknown status";
+}
+
+int tqkv_last_cuda_error(void) { return tqkv::t_last_cuda_error; }
+
+const char* tqkv_version(void) { return "tqkv-b200 0.1.0 sm_100a"; }
+
+tqkv_status tqkv_kv_compress(const void* x, int8_t* xq, void* scales, int B, int H, int S, int D,
+                             int block_size, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S <= 0) return TQKV_ERR_INVALID_SIZE;
+    if (!x || !xq || !scales) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(x) || !tqkv::aligned16(xq)) return TQKV_ERR_MISALIGNED;
+    const long long rows = static_cast<long long>(B) * H * S;
+    return tqkv::launch_compress(x, xq, scales, rows, D, block_size, stream);
+}
+
+tqkv_status tqkv_kv_reconstruct(const int8_t* xq, const void* scales, void* y, int B, int H,
+                                int S, int D, int block_size, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S <= 0) return TQKV_ERR_INVALID_SIZE;
+    if (!xq || !scales || !y) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(xq) || !tqkv::aligned16(y)) return TQKV_ERR_MISALIGNED;
+    const long long rows = static_cast<long long>(B) * H * S;
+    return tqkv::launch_reconstruct(xq, scales, y, rows, D, block_size, stream);
+}
+
+size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D) {
+    if (B <= 0 || H <= 0 || S <= 0 || (D != 64 && D != 128)) return 0;
+    return tqkv::decode_workspace_bytes(static_cast<long long>(B) * H, S, D);
+}
+
+tqkv_status tqkv_workspace_init(void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (workspace_bytes == 0) return TQKV_OK;
+    if (!workspace) return TQKV_ERR_NULL;
+    return tqkv::from_cuda(cudaMemsetAsync(workspace, 0, workspace_bytes, stream));
+}
+
+tqkv_status tqkv_decode_int8(const void* q, const int8_t* kq, const void* ks, const int8_t* vq,
+                             const void* vs, void* o, int B, int H, int S, int D, int block_size,
+                             void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S < 0) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_fill_half(o, BH * D, 0x7e00u, stream);  // NaN, as 0 * (1/0)
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode(KvKind::kInt8, OutKind::kHalfO, q, kq, ks, vq, vs, o,
+                               static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
+                               stream);
+}
+
+tqkv_status tqkv_decode_fp16(const void* q, const void* k, const void* v, void* o, int B, int H,
+                             int S, int D, void* workspace, size_t workspace_bytes,
+                             cudaStream_t stream) {
+    if (D != 64 && D != 128) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S < 0) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_fill_half(o, BH * D, 0x0000u, stream);
+    if (!k || !v) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(k) || !tqkv::aligned16(v)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode(KvKind::kHalf, OutKind::kHalfO, q, k, nullptr, v, nullptr, o,
+                               static_cast<int>(BH), S, D, D, workspace, workspace_bytes, stream);
+}
+
+tqkv_status tqkv_decode_int8_partial(const void* q, const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs, float* partial, int B,
+                                     int H, int S, int D, int block_size, void* workspace,
+                                     size_t workspace_bytes, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S < 0) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !partial) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_empty_partials(partial, BH, D, stream);
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode(KvKind::kInt8, OutKind::kPartial, q, kq, ks, vq, vs, partial,
+                               static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
+                               stream);
+}
+
+tqkv_status tqkv_lse_combine(const float* partials, void* o, int R, int BH, int D,
+                             cudaStream_t stream) {
+    if (D != 64 && D != 128) return TQKV_ERR_UNSUPPORTED;
+    if (R <= 0 || BH <= 0) return TQKV_ERR_INVALID_SIZE;
+    if (!partials || !o) return TQKV_ERR_NULL;
+    if (D == 64) return tqkv::combine_impl<64>(partials, o, R, BH, stream);
+    return tqkv::combine_impl<128>(partials, o, R, BH, stream);
+}
+
+tqkv_status tqkv_read_device_error(uint32_t* code_out) {
+    if (!code_out) return TQKV_ERR_NULL;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, tqkv::g_device_error, sizeof(v));
+    if (e != cudaSuccess) return tqkv::from_cuda(e);
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(tqkv::g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return tqkv::from_cuda(e);
+    *code_out = v;
+    return TQKV_OK;
+}
+
+}  // extern "C"

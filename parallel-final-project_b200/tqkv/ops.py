@@ -1,0 +1,177 @@
+"""Torch-tensor front end of the C ABI (include/tqkv.h).
+
+Every function takes CUDA tensors in the reference's layouts
+(reference include/quantization.h:5-12, include/attention.h):
+
+    q, o     fp16 [B, H, D]
+    k, v     fp16 [B, H, S, D]
+    kq, vq   int8 [B, H, S, D]
+    ks, vs   fp16 [B, H, S, D // block_size]
+
+and launches on the current torch stream (or `stream=`).  Torch only
+allocates memory and provides streams here; all compute is the library's
+sm_100a kernels.  Errors raise TqkvError.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from ._lib import check, load
+
+_F16 = torch.float16
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(stream: Optional[torch.cuda.Stream]) -> int:
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream
+
+
+def _bhsd(t: torch.Tensor, name: str) -> Tuple[int, int, int, int]:
+    if t.dim() != 4 or not t.is_contiguous() or not t.is_cuda:
+        raise ValueError(f"{name} must be a contiguous CUDA tensor [B, H, S, D]")
+    return tuple(t.shape)  # type: ignore[return-value]
+
+
+def kv_compress(x: torch.Tensor, block_size: int, xq: Optional[torch.Tensor] = None,
+                scales: Optional[torch.Tensor] = None, stream=None):
+    """Kernel A: fp16 [B,H,S,D] -> (int8 codes [B,H,S,D], fp16 scales [B,H,S,D/bs])."""
+    if x.dtype != _F16:
+        raise ValueError("x must be fp16")
+    B, H, S, D = _bhsd(x, "x")
+    if xq is None:
+        xq = torch.empty((B, H, S, D), dtype=torch.int8, device=x.device)
+    if scales is None:
+        scales = torch.empty((B, H, S, max(D // block_size, 1)), dtype=_F16, device=x.device)
+    lib = load()
+    check("tqkv_kv_compress", lib.tqkv_kv_compress(
+        _ptr(x), _ptr(xq), _ptr(scales), B, H, S, D, block_size, _stream_handle(stream)))
+    return xq, scales
+
+
+def kv_reconstruct(xq: torch.Tensor, scales: torch.Tensor, block_size: int,
+                   y: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Kernel B: codes + scales -> fp16 [B,H,S,D]."""
+    B, H, S, D = _bhsd(xq, "xq")
+    if y is None:
+        y = torch.empty((B, H, S, D), dtype=_F16, device=xq.device)
+    lib = load()
+    check("tqkv_kv_reconstruct", lib.tqkv_kv_reconstruct(
+        _ptr(xq), _ptr(scales), _ptr(y), B, H, S, D, block_size, _stream_handle(stream)))
+    return y
+
+
+def workspace_bytes(B: int, H: int, S: int, D: int) -> int:
+    """Scratch the decode kernels need for this shape on the current device."""
+    return int(load().tqkv_decode_workspace_bytes(B, H, S, D))
+
+
+class Workspace:
+    """A zero-initialised decode workspace on one device, grown on demand.
+
+    The kernels leave it zeroed after every call, so one Workspace can serve
+    any number of calls that are ordered on the same stream.
+    """
+
+    def __init__(self, device=None):
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.buf: Optional[torch.Tensor] = None
+
+    def get(self, nbytes: int, stream=None) -> Tuple[Optional[int], int]:
+        if nbytes == 0:
+            return None, 0
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            lib = load()
+            check("tqkv_workspace_init", lib.tqkv_workspace_init(
+                self.buf.data_ptr(), nbytes, _stream_handle(stream)))
+        return self.buf.data_ptr(), self.buf.numel()
+
+
+_default_ws: dict = {}
+
+
+def _workspace(ws: Optional[Workspace], device: torch.device) -> Workspace:
+    if ws is not None:
+        return ws
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    if key not in _default_ws:
+        _default_ws[key] = Workspace(device)
+    return _default_ws[key]
+
+
+def decode_int8(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor,
+                vs: torch.Tensor, block_size: int, out: Optional[torch.Tensor] = None,
+                workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Kernel D: fused INT8 decode attention -> O fp16 [B,H,D]."""
+    B, H, S, D = _bhsd(kq, "kq")
+    if out is None:
+        out = torch.empty((B, H, D), dtype=_F16, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
+    lib = load()
+    check("tqkv_decode_int8", lib.tqkv_decode_int8(
+        _ptr(q), _ptr(kq), _ptr(ks), _ptr(vq), _ptr(vs), _ptr(out), B, H, S, D, block_size,
+        wptr, wbytes, _stream_handle(stream)))
+    return out
+
+
+def decode_fp16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: Optional[torch.Tensor] = None, workspace: Optional[Workspace] = None,
+                stream=None) -> torch.Tensor:
+    """FP16 decode attention (the reference's baseline) -> O fp16 [B,H,D]."""
+    B, H, S, D = _bhsd(k, "k")
+    if out is None:
+        out = torch.empty((B, H, D), dtype=_F16, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
+    lib = load()
+    check("tqkv_decode_fp16", lib.tqkv_decode_fp16(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, S, D, wptr, wbytes,
+        _stream_handle(stream)))
+    return out
+
+
+def decode_int8_partial(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor,
+                        vs: torch.Tensor, block_size: int, out: Optional[torch.Tensor] = None,
+                        workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Per-head split-S partial records over this device's token slice:
+    float32 [B*H, D+2] = (acc[0..D-1], m, l), natural-log units."""
+    B, H, S, D = _bhsd(kq, "kq")
+    if out is None:
+        out = torch.empty((B * H, D + 2), dtype=torch.float32, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H, S, D) if S > 0 else 0, stream)
+    lib = load()
+    check("tqkv_decode_int8_partial", lib.tqkv_decode_int8_partial(
+        _ptr(q), _ptr(kq), _ptr(ks), _ptr(vq), _ptr(vs), _ptr(out), B, H, S, D, block_size,
+        wptr, wbytes, _stream_handle(stream)))
+    return out
+
+
+def lse_combine(partials: torch.Tensor, D: int, out: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+    """Merge R partial-record sets [R, BH, D+2] into O fp16 [BH, D]."""
+    if partials.dim() != 3 or partials.shape[2] != D + 2 or partials.dtype != torch.float32:
+        raise ValueError("partials must be float32 [R, BH, D + 2]")
+    R, BH = partials.shape[0], partials.shape[1]
+    if out is None:
+        out = torch.empty((BH, D), dtype=_F16, device=partials.device)
+    lib = load()
+    check("tqkv_lse_combine", lib.tqkv_lse_combine(
+        _ptr(partials), _ptr(out), R, BH, D, _stream_handle(stream)))
+    return out
+
+
+def read_device_error() -> int:
+    """Read and clear the device-side bounded-wait failure flag (0 = none)."""
+    code = ctypes.c_uint32(0)
+    check("tqkv_read_device_error", load().tqkv_read_device_error(ctypes.byref(code)))
+    return int(code.value)

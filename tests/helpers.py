@@ -1,0 +1,23 @@
+"""Helpers shared by the GPU parity tests (device tensors <-> oracle)."""
+import numpy as np
+import torch
+
+from oracle import oracle as O
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy()
+
+
+def oracle_int8_reference(q, kq, ks, vq, vs, bs):
+    """Oracle output (float32 [B,H,D]) on the dequantised K/V, as the
+    reference's check computes it (python/check_correctness.py:121-129)."""
+    kd = O.dequantize(to_np(kq), to_np(ks), bs)
+    vd = O.dequantize(to_np(vq), to_np(vs), bs)
+    return O.attention(to_np(q).astype(np.float32), kd, vd)
+
+
+def max_abs(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.max(np.abs(a - b))) if a.size else 0.0
