@@ -98,6 +98,7 @@ class ClockSampler:
 
     def __init__(self, device_index: int, interval_s: float = 0.002):
         self.samples, self.reasons = [], set()
+        self.mem_mhz, self.power_w = [], []
         self.max_mhz = None
         self.interval = interval_s
         self._stop = threading.Event()
@@ -116,6 +117,8 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.mem_mhz.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_MEM))
+                self.power_w.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
                 mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 for bit, name in self.REASONS.items():
                     if mask & bit and name != "gpu_idle":
@@ -140,6 +143,9 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
                     "samples": 0}
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(self.samples), "mem_mhz": statistics.median(self.mem_mhz),
+                "power_w_median": statistics.median(self.power_w),
+                "power_w_max": max(self.power_w),
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
@@ -301,10 +307,12 @@ def main():
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("tqkv_timed")  # lets ncu --nvtx-include select this region
         ev0.record()
         for i in range(args.steps):
             step(kev[i])
         ev1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     barrier()
     step_ms_local = ev0.elapsed_time(ev1) / args.steps

@@ -56,7 +56,7 @@ constexpr int kDecodeConsumerWarps = 4;
 constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
 constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeTileBytes = 8192;  // bytes of K (and of V) per stage
-constexpr int kDecodeStages = 4;
+constexpr int kDecodeStages = 3;        // 3 stages x ~17.7 KB: four CTAs fit on an SM
 constexpr int kMergeBarrier = 1;        // named barrier id used by consumers
 
 enum DecodeOut : int {
@@ -272,9 +272,10 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
 template <int D, int BS, bool kHalfKV>
 struct SegState {
     using C = DecodeCfg<D, BS, kHalfKV>;
-    float m2;             // running max of base-2 scores
+    float m2;             // reference max of base-2 scores (raised lazily, see kLazyRescale)
+    float mx;             // true running max of base-2 scores
     float l;              // running sum of 2^(s - m2)
-    float acc[C::kEPL];   // running sum of 2^(s - m2) * v over this lane's dims
+    float2 acc[C::kEPL / 2];  // running sum of 2^(s - m2) * v over this lane's dims (pairs)
     // INT8: q as fixed point, high and low bytes, 4 dims per word
     int qh[4];
     uint32_t ql[4];
@@ -342,18 +343,22 @@ __device__ __forceinline__ void load_q(SegState<D, BS, kHalfKV>& st, const uint8
         st.cq = inv * score_scale_log2;
     }
     st.m2 = -INFINITY;
+    st.mx = -INFINITY;
     st.l = 0.0f;
 #pragma unroll
-    for (int i = 0; i < C::kEPL; ++i) st.acc[i] = 0.0f;
+    for (int i = 0; i < C::kEPL / 2; ++i) st.acc[i] = make_float2(0.0f, 0.0f);
 }
 
 
-// Exact int8 -> fp32 of byte b of a word already XOR-ed with 0x80808080:
-// the float with bits 0x4B0000uu is 2^23 + uu, and uu = code + 128.
+// Exact int8 -> fp32 of bytes b and b+1 of a word already XOR-ed with
+// 0x80808080: the float with bits 0x4B0000uu is 2^23 + uu, uu = code + 128,
+// so one packed subtraction of (2^23 + 128) leaves the two codes exactly.
 template <int b>
-__device__ __forceinline__ float biased_byte_to_float(uint32_t u) {
-    return __int_as_float(static_cast<int>(__byte_perm(u, 0x4B000000u, 0x7440u + b))) -
-           8388736.0f;
+__device__ __forceinline__ float2 biased_bytes_to_float2(uint32_t u) {
+    const float2 f = make_float2(
+        __int_as_float(static_cast<int>(__byte_perm(u, 0x4B000000u, 0x7440u + b))),
+        __int_as_float(static_cast<int>(__byte_perm(u, 0x4B000000u, 0x7440u + b + 1))));
+    return __fadd2_rn(f, make_float2(-8388736.0f, -8388736.0f));
 }
 
 // Shared-memory byte offset, inside a stage's scale slot, of the first scale
@@ -363,23 +368,65 @@ __device__ __forceinline__ int scale_slot_offset(const uint16_t* base, long long
     return static_cast<int>((reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(row0) * nsub * 2) & 15);
 }
 
+// Reduce-scatter of four per-lane partials (one per token of the lane group)
+// over the LPR lanes of a group: afterwards lane r holds the full sum of
+// token  ((r & LPR/2) ? 2 : 0) + ((r & LPR/4) ? 1 : 0).  Two halving stages
+// move 2 + 1 values per lane, the remaining stages 1 value: 4 + log2(LPR/4)
+// shuffles instead of 4 * log2(LPR) for four all-reduces.
+template <int LPR, typename T>
+__device__ __forceinline__ T reduce_scatter4(T v0, T v1, T v2, T v3, int r) {
+    constexpr int h = LPR / 2, q = LPR / 4;
+    const bool up = (r & h) != 0;
+    T k0 = up ? v2 : v0, k1 = up ? v3 : v1;
+    const T s0 = up ? v0 : v2, s1 = up ? v1 : v3;
+    k0 += __shfl_xor_sync(0xffffffffu, s0, h);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, h);
+    const bool odd = (r & q) != 0;
+    T k = odd ? k1 : k0;
+    k += __shfl_xor_sync(0xffffffffu, odd ? k0 : k1, q);
+#pragma unroll
+    for (int off = q / 2; off >= 1; off >>= 1) k += __shfl_xor_sync(0xffffffffu, k, off);
+    return k;
+}
+
+// Token of the group (0..3) whose full sum lane r holds after reduce_scatter4,
+// and the first lane holding token j.
+template <int LPR>
+__device__ __forceinline__ int scattered_token(int r) {
+    return ((r & (LPR / 2)) ? 2 : 0) + ((r & (LPR / 4)) ? 1 : 0);
+}
+template <int LPR>
+__device__ __forceinline__ int holder_lane(int j) {
+    return (j >> 1) * (LPR / 2) + (j & 1) * (LPR / 4);
+}
+
+// The running max is only raised when a tile's max exceeds it by more than
+// 2^kLazyRescale: until then 2^(s - m2) <= 2^kLazyRescale stays well inside
+// fp32 and acc / l keep their scale, so the rescale of acc (EPL multiplies
+// per lane) is skipped on almost every tile.
+constexpr float kLazyRescale = 8.0f;
+
 template <int D, int BS, bool kHalfKV>
 __device__ __forceinline__ void consume_tile(SegState<D, BS, kHalfKV>& st, const uint8_t* stage,
                                              int cnt, int ks_off, int vs_off, int g, int r) {
     using C = DecodeCfg<D, BS, kHalfKV>;
-    constexpr int kTPG = C::kTPG;
-    int rows[kTPG];
+    constexpr int kLPR = C::kLPR;
+    const int lane = threadIdx.x & 31;
+    const int gbase = lane - r;  // first lane of this group in the warp
+    int rows[4];
 #pragma unroll
-    for (int j = 0; j < kTPG; ++j) rows[j] = g + C::kGroups * j;
+    for (int j = 0; j < 4; ++j) rows[j] = g + C::kGroups * j;
+    const int tj = scattered_token<kLPR>(r);
+    const int row_own = g + C::kGroups * tj;
+    const bool valid_own = row_own < cnt;
 
-    // ---- scores, base 2 ----
-    float s[kTPG];
+    // ---- scores, base 2: lane r ends with the score of its own token tj ----
+    float s;
     if constexpr (!kHalfKV) {
         const uint8_t* ksm = stage + C::kOffKS + ks_off;
-        const int blk = (16 * r) / BS;
-        int dot[kTPG];
+        int dot[4];
 #pragma unroll
-        for (int j = 0; j < kTPG; ++j) {
+        for (int j = 0; j < 4; ++j) {
             const uint4 kw = lds128(stage + C::kOffK + rows[j] * C::kRowBytes + 16 * r);
             int h = dp4a_ss(static_cast<int>(kw.x), st.qh[0], 0);
             h = dp4a_ss(static_cast<int>(kw.y), st.qh[1], h);
@@ -392,112 +439,103 @@ __device__ __forceinline__ void consume_tile(SegState<D, BS, kHalfKV>& st, const
             dot[j] = t;
         }
         if constexpr (C::kNSub == 1) {
-            // one scale per row: reduce the exact integers, then scale once
-#pragma unroll
-            for (int off = 1; off < C::kLPR; off <<= 1) {
-#pragma unroll
-                for (int j = 0; j < kTPG; ++j) dot[j] += __shfl_xor_sync(0xffffffffu, dot[j], off);
-            }
-#pragma unroll
-            for (int j = 0; j < kTPG; ++j) {
-                const float ks = half_bits_to_float(
-                    *reinterpret_cast<const uint16_t*>(ksm + 2 * rows[j]));
-                s[j] = static_cast<float>(dot[j]) * (ks * st.cq);
-            }
+            // one scale per row: reduce exact integers, scale once
+            const int tot = reduce_scatter4<kLPR>(dot[0], dot[1], dot[2], dot[3], r);
+            const float ks = half_bits_to_float(*reinterpret_cast<const uint16_t*>(ksm + 2 * row_own));
+            s = static_cast<float>(tot) * (ks * st.cq);
         } else {
-            // several blocks per row: scale each lane's block partial, then reduce
+            // several blocks per row: scale each lane's block partial first
+            const int blk = (16 * r) / BS;
+            float f[4];
 #pragma unroll
-            for (int j = 0; j < kTPG; ++j) {
+            for (int j = 0; j < 4; ++j) {
                 const float ks = half_bits_to_float(*reinterpret_cast<const uint16_t*>(
                     ksm + 2 * (rows[j] * C::kNSub + blk)));
-                s[j] = static_cast<float>(dot[j]) * ks;
+                f[j] = static_cast<float>(dot[j]) * ks;
             }
-#pragma unroll
-            for (int off = 1; off < C::kLPR; off <<= 1) {
-#pragma unroll
-                for (int j = 0; j < kTPG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
-            }
-#pragma unroll
-            for (int j = 0; j < kTPG; ++j) s[j] *= st.cq;
+            s = reduce_scatter4<kLPR>(f[0], f[1], f[2], f[3], r) * st.cq;
         }
     } else {
+        float d[4];
 #pragma unroll
-        for (int j = 0; j < kTPG; ++j) {
+        for (int j = 0; j < 4; ++j) {
             const uint4 kw = lds128(stage + C::kOffK + rows[j] * C::kRowBytes + 16 * r);
             const uint32_t w[4] = {kw.x, kw.y, kw.z, kw.w};
-            float d = 0.0f;
+            float2 a = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-                d = fmaf(st.qf[2 * i], kf.x, d);
-                d = fmaf(st.qf[2 * i + 1], kf.y, d);
-            }
-            s[j] = d;
+            for (int i = 0; i < 4; ++i)
+                a = __ffma2_rn(make_float2(st.qf[2 * i], st.qf[2 * i + 1]),
+                               __half22float2(*reinterpret_cast<const __half2*>(&w[i])), a);
+            d[j] = a.x + a.y;
         }
-#pragma unroll
-        for (int off = 1; off < C::kLPR; off <<= 1) {
-#pragma unroll
-            for (int j = 0; j < kTPG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
-        }
-#pragma unroll
-        for (int j = 0; j < kTPG; ++j) s[j] *= st.cq;
+        s = reduce_scatter4<kLPR>(d[0], d[1], d[2], d[3], r) * st.cq;
     }
-#pragma unroll
-    for (int j = 0; j < kTPG; ++j) s[j] = rows[j] < cnt ? s[j] : -INFINITY;
+    s = valid_own ? s : -INFINITY;
 
-    // ---- online softmax update (base 2) ----
-    float mt = s[0];
+    // ---- online softmax over the group's 4 tokens (base 2, lazy rescale) ----
+    float mt = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, kLPR / 4));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, kLPR / 2));
+    st.mx = fmaxf(st.mx, mt);
+    const bool raise = mt > st.m2 + kLazyRescale;  // false while mt == -inf
+    if (__any_sync(0xffffffffu, raise)) {            // warp-uniform, rare
+        const float m_new = raise ? mt : st.m2;
+        const float alpha = raise ? fast_exp2(st.m2 - m_new) : 1.0f;  // 2^-inf = 0
+        st.l *= alpha;
 #pragma unroll
-    for (int j = 1; j < kTPG; ++j) mt = fmaxf(mt, s[j]);
-    const float m_new = fmaxf(st.m2, mt);
-    const float base = m_new == -INFINITY ? 0.0f : m_new;  // nothing seen yet: all terms 0
-    const float alpha = fast_exp2(st.m2 - base);
-    float e[kTPG];
-    float esum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kTPG; ++j) {
-        e[j] = fast_exp2(s[j] - base);
-        esum += e[j];
+        for (int i = 0; i < C::kEPL / 2; ++i) st.acc[i] = __fmul2_rn(st.acc[i], make_float2(alpha, alpha));
+        st.m2 = m_new;
     }
-    st.l = st.l * alpha + esum;
-    st.m2 = m_new;
-#pragma unroll
-    for (int i = 0; i < C::kEPL; ++i) st.acc[i] *= alpha;
+    const float base = st.m2 == -INFINITY ? 0.0f : st.m2;
+    const float e = fast_exp2(s - base);  // 0 for masked rows
+    float es = e + __shfl_xor_sync(0xffffffffu, e, kLPR / 4);
+    es += __shfl_xor_sync(0xffffffffu, es, kLPR / 2);
+    st.l += es;
 
     // ---- weighted V ----
+    float w[4];
     if constexpr (!kHalfKV) {
         const uint8_t* vsm = stage + C::kOffVS + vs_off;
-        const int blk = (16 * r) / BS;
+        if constexpr (C::kNSub == 1) {
+            const float vsc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(vsm + 2 * row_own));
+            const float w_own = valid_own ? e * vsc : 0.0f;  // stale rows: weight exactly 0
 #pragma unroll
-        for (int j = 0; j < kTPG; ++j) {
-            const float vsc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(
-                vsm + 2 * (rows[j] * C::kNSub + blk)));
-            // rows past cnt hold stale bytes (finite codes) and maybe a stale
-            // scale; their weight is forced to exactly 0.
-            const float w = rows[j] < cnt ? e[j] * vsc : 0.0f;
+            for (int j = 0; j < 4; ++j)
+                w[j] = __shfl_sync(0xffffffffu, w_own, gbase + holder_lane<kLPR>(j));
+        } else {
+            const int blk = (16 * r) / BS;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float ej = __shfl_sync(0xffffffffu, e, gbase + holder_lane<kLPR>(j));
+                const float vsc = half_bits_to_float(*reinterpret_cast<const uint16_t*>(
+                    vsm + 2 * (rows[j] * C::kNSub + blk)));
+                w[j] = rows[j] < cnt ? ej * vsc : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
             const uint4 vw = lds128(stage + C::kOffV + rows[j] * C::kRowBytes + 16 * r);
             const uint32_t u[4] = {vw.x ^ 0x80808080u, vw.y ^ 0x80808080u, vw.z ^ 0x80808080u,
                                    vw.w ^ 0x80808080u};
+            const float2 ww = make_float2(w[j], w[j]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                st.acc[4 * i + 0] = fmaf(w, biased_byte_to_float<0>(u[i]), st.acc[4 * i + 0]);
-                st.acc[4 * i + 1] = fmaf(w, biased_byte_to_float<1>(u[i]), st.acc[4 * i + 1]);
-                st.acc[4 * i + 2] = fmaf(w, biased_byte_to_float<2>(u[i]), st.acc[4 * i + 2]);
-                st.acc[4 * i + 3] = fmaf(w, biased_byte_to_float<3>(u[i]), st.acc[4 * i + 3]);
+                st.acc[2 * i] = __ffma2_rn(ww, biased_bytes_to_float2<0>(u[i]), st.acc[2 * i]);
+                st.acc[2 * i + 1] = __ffma2_rn(ww, biased_bytes_to_float2<2>(u[i]), st.acc[2 * i + 1]);
             }
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < kTPG; ++j) {
+        for (int j = 0; j < 4; ++j) w[j] = __shfl_sync(0xffffffffu, e, gbase + holder_lane<kLPR>(j));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
             if (rows[j] < cnt) {  // stale fp16 rows may hold Inf/NaN: skip, do not weight by 0
                 const uint4 vw = lds128(stage + C::kOffV + rows[j] * C::kRowBytes + 16 * r);
                 const uint32_t w4[4] = {vw.x, vw.y, vw.z, vw.w};
+                const float2 ww = make_float2(w[j], w[j]);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
-                    st.acc[2 * i] = fmaf(e[j], vf.x, st.acc[2 * i]);
-                    st.acc[2 * i + 1] = fmaf(e[j], vf.y, st.acc[2 * i + 1]);
-                }
+                for (int i = 0; i < 4; ++i)
+                    st.acc[i] = __ffma2_rn(ww, __half22float2(*reinterpret_cast<const __half2*>(&w4[i])),
+                                           st.acc[i]);
             }
         }
     }
@@ -521,6 +559,15 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
     using C = DecodeCfg<D, BS, kHalfKV>;
     const int lane = tid & 31;
     const int warp = tid >> 5;
+    // 0) move each group's reference max to its true max, so that records
+    //    carry m = max_t s_t (the lazy rescale let m2 lag behind by < 2^8)
+    {
+        const float alpha = st.mx == -INFINITY ? 1.0f : fast_exp2(st.m2 - st.mx);
+        st.l *= alpha;
+#pragma unroll
+        for (int i = 0; i < C::kEPL / 2; ++i) st.acc[i] = __fmul2_rn(st.acc[i], make_float2(alpha, alpha));
+        st.m2 = st.mx;
+    }
     // 1) lane groups inside a warp: lanes l, l + LPR, ... hold the same dims
 #pragma unroll
     for (int off = C::kLPR; off < 32; off <<= 1) {
@@ -530,9 +577,12 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
         lse_factors(st.m2, mo, M, fa, fb);
         st.l = st.l * fa + lo * fb;
 #pragma unroll
-        for (int i = 0; i < C::kEPL; ++i) {
-            const float ao = __shfl_xor_sync(0xffffffffu, st.acc[i], off);
-            st.acc[i] = st.acc[i] * fa + ao * fb;
+        for (int i = 0; i < C::kEPL / 2; ++i) {
+            float2 ao;
+            ao.x = __shfl_xor_sync(0xffffffffu, st.acc[i].x, off);
+            ao.y = __shfl_xor_sync(0xffffffffu, st.acc[i].y, off);
+            st.acc[i] = __ffma2_rn(st.acc[i], make_float2(fa, fa),
+                                   __fmul2_rn(ao, make_float2(fb, fb)));
         }
         st.m2 = M;
     }
@@ -540,7 +590,10 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
     float* mw = merge + warp * (D + 2);
     if (lane < C::kLPR) {
 #pragma unroll
-        for (int i = 0; i < C::kEPL; ++i) mw[lane * C::kEPL + i] = st.acc[i];
+        for (int i = 0; i < C::kEPL / 2; ++i) {
+            mw[lane * C::kEPL + 2 * i] = st.acc[i].x;
+            mw[lane * C::kEPL + 2 * i + 1] = st.acc[i].y;
+        }
         if (lane == 0) {
             mw[D] = st.m2;
             mw[D + 1] = st.l;
@@ -621,14 +674,21 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
                 }
             }
         }
-        if (tid == 0) a.tickets[bh] = 0u;  // leave the workspace zeroed for the next call
+        // leave the workspace all-zero for the next call, whatever its shape:
+        // the ticket, and every record this merge consumed
+        named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+        float* zrec = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
+        for (int i = tid; i < nparts * (D + 2); i += kDecodeConsumers) zrec[i] = 0.0f;
+        if (tid == 0) a.tickets[bh] = 0u;
     }
     named_barrier_sync(kMergeBarrier, kDecodeConsumers);
 }
 
 // ---------------------------------------------------------------------------
+constexpr int kDecodeCtasPerSm = 4;  // target residency (smem: 3 stages; regs: <= 102 per thread)
+
 template <int D, int BS, bool kHalfKV, int OUT>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     decode_attn_kernel(const DecodeArgs a) {
     using C = DecodeCfg<D, BS, kHalfKV>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -696,9 +756,10 @@ __global__ void __launch_bounds__(kDecodeThreads)
                 consume_tile<D, BS, kHalfKV>(st, sp, cnt, ks_off, vs_off, g, r);
             } else if (t0 == t_a) {
                 st.m2 = -INFINITY;
+                st.mx = -INFINITY;
                 st.l = 0.0f;
 #pragma unroll
-                for (int i = 0; i < C::kEPL; ++i) st.acc[i] = 0.0f;
+                for (int i = 0; i < C::kEPL / 2; ++i) st.acc[i] = make_float2(0.0f, 0.0f);
             }
             __syncwarp();
             if (lane == 0 && !broken) mbar_arrive(&empty[stage]);

@@ -55,10 +55,10 @@ def test_int8_decode_full_config(name):
     kq, ks, vq, vs = _compress_kv(k, v, w.block_size)
     o = tqkv.decode_int8(q, kq, ks, vq, vs, w.block_size)
     torch.cuda.synchronize()
-    ref = oracle_int8_reference(q, kq, ks, vq, vs, w.block_size)
+    ref = oracle_int8_reference(q, kq, ks, vq, vs, w.block_size, exact=False)
     err = max_abs(to_np(o), ref)
     assert err < REF_TOL, err
-    assert_tight(to_np(o), ref)
+    assert_tight(to_np(o), oracle_int8_reference(q, kq, ks, vq, vs, w.block_size))
     assert tqkv.read_device_error() == 0
 
 
@@ -221,8 +221,24 @@ def test_workspace_left_zeroed():
     torch.cuda.synchronize()
     nb = tqkv.workspace_bytes(B, H, S, D)
     assert nb > 0
-    # ticket counters sit at the start of the workspace
-    assert int(ws.buf[:256].count_nonzero()) == 0
+    # tickets and every partial record: the whole workspace is zero again
+    assert int(ws.buf.count_nonzero()) == 0
+
+
+def test_workspace_reused_across_shapes():
+    """One workspace serves calls of different shapes in any order: a call's
+    ticket counters never see records left by an earlier, smaller call."""
+    ws = tqkv.Workspace()
+    shapes = [(1, 2, 40000, 128, 128), (8, 12, 3000, 64, 64), (1, 1, 90000, 128, 32),
+              (4, 32, 2500, 128, 64), (1, 3, 70000, 64, 32)]
+    for i, (B, H, S, D, bs) in enumerate(shapes):
+        q = _rand((B, H, D), 100 + i)
+        k, v = _rand((B, H, S, D), 200 + i), _rand((B, H, S, D), 300 + i)
+        kq, ks, vq, vs = _compress_kv(k, v, bs)
+        o = tqkv.decode_int8(q, kq, ks, vq, vs, bs, workspace=ws)
+        torch.cuda.synchronize()
+        assert_tight(to_np(o), oracle_int8_reference(q, kq, ks, vq, vs, bs))
+        assert int(ws.buf.count_nonzero()) == 0
 
 
 def test_repeat_calls_identical():
@@ -235,3 +251,37 @@ def test_repeat_calls_identical():
         o2 = tqkv.decode_int8(q, kq, ks, vq, vs, w.block_size)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
+
+
+def _golden():
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                        "ref_build_golden.json")
+    with open(path) as f:
+        return json.load(f)["cases"]
+
+
+@pytest.mark.parametrize("name", ["fp16_small", "int8_b2h8", "int8_gpt2_outlier",
+                                  "int8_bs32_lognormal", "int8_bs128_ragged"])
+def test_decode_vs_reference_kernels_golden(name):
+    """Outputs of the reference's own kernels (online Kernel D, two-pass
+    Kernel C, fp16 baseline), recorded on the same inputs: ours agree to well
+    inside the 1e-2 contract."""
+    import golden.gen as gen
+    case = _golden()[name]
+    q, k, v = (torch.from_numpy(a).cuda() for a in gen.inputs(name))
+    bs = case["block_size"]
+    if bs == 0:
+        o = tqkv.decode_fp16(q, k, v)
+        refs = [case["O_baseline_bits"]]
+    else:
+        kq, ks, vq, vs = _compress_kv(k, v, bs)
+        o = tqkv.decode_int8(q, kq, ks, vq, vs, bs)
+        refs = [case["O_online_bits"], case["O_fused_bits"]]
+    torch.cuda.synchronize()
+    got = to_np(o).reshape(-1).astype(np.float64)
+    for bits in refs:
+        ref = np.asarray(bits, np.uint16).view(np.float16).astype(np.float64)
+        assert max_abs(got, ref) < REF_TOL
+        assert_tight(got, ref)
