@@ -19,7 +19,7 @@ void launch_decode_attn_baseline(
     cudaStream_t stream);
 
 // INT8 decode attention with in-register dequantisation; replaces reference
-// src/attention_int8_fused.cu:316-346 (its two-pass softmax and S <= ~12k
+// src/attention_int8_fused.cu:161-191 (its two-pass softmax and S <= ~12k
 // limit are gone; the output is the same function).
 void launch_decode_attn_int8_fused(
     const __half* dQ,

@@ -18,7 +18,7 @@ void launch_kv_compress(
     int B, int H, int S, int D, int block_size,
     cudaStream_t stream);
 
-// Kernel B; replaces reference src/kv_reconstruct.cu:36-62.
+// Kernel B; replaces reference src/kv_reconstruct.cu:38-62.
 void launch_kv_reconstruct(
     const int8_t* dXq, const __half* dScales, __half* dY,
     int B, int H, int S, int D, int block_size,

@@ -6,8 +6,8 @@
 //     on first use and is then reused);
 //   * an unsupported (D, block_size, lanes, tile) prints a message to stderr
 //     and calls std::abort() (reference src/kv_compress.cu:130-135,
-//     src/kv_reconstruct.cu:44-50, src/attention_baseline.cu:151-154,
-//     src/attention_int8_fused.cu:340-345,
+//     src/kv_reconstruct.cu:45-50, src/attention_baseline.cu:151-154,
+//     src/attention_int8_fused.cu:185-190,
 //     src/attention_int8_fused_online.cu:234-238);
 //   * an empty grid (B*H*S == 0 for the row kernels, B or H == 0 for
 //     attention) leaves cudaErrorInvalidConfiguration pending, and launch

@@ -1,0 +1,135 @@
+"""CPU model of the decode kernel's schedule and memory accesses.
+
+Compute-sanitizer is not available for this kernel's GPU runs, so its bounds
+are established here instead: the host plan (make_plan in tqkv_capi.cu), the
+producer's tile loop and bulk-copy spans, the consumers' shared-memory reads
+and the workspace part indices (decode_attn.cuh) are re-enacted for many
+shapes, asserting that
+  * every token row of every head is covered exactly once;
+  * every bulk copy is 16-byte aligned, a multiple of 16 bytes, inside its
+    global buffer and inside its shared-memory slot;
+  * every plain edge load is inside its buffer and its slot;
+  * every consumer read of scales and q stays inside the stage;
+  * part indices stay below max_parts of the workspace layout.
+The tile size, stage count and planning constants are read from the sources,
+so the model follows the code."""
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(REPO, "parallel-final-project_b200", "csrc")
+
+
+def _const(path, name):
+    src = open(os.path.join(CSRC, path)).read()
+    m = re.search(rf"constexpr\s+(?:long long|int)\s+{name}\s*=\s*([0-9]+)", src)
+    assert m, name
+    return int(m.group(1))
+
+
+TILE_BYTES = _const("decode_attn.cuh", "kDecodeTileBytes")
+STAGES = _const("decode_attn.cuh", "kDecodeStages")
+WARPS = _const("decode_attn.cuh", "kDecodeConsumerWarps")
+MIN_ROWS = _const("tqkv_capi.cu", "kMinRowsPerCta")
+BOUND_OCC = _const("tqkv_capi.cu", "kMaxCtasPerSmBound")
+SMS = 148
+
+
+def make_plan(total, S, max_ctas):
+    g = max(min(-(-total // MIN_ROWS), max_ctas), 1)
+    r = -(-total // g)
+    r = -(-r // 16) * 16
+    return -(-total // r), r, (S - 1) // r + 2
+
+
+def plan_span(src, n, lo, hi):
+    a16 = src & ~15
+    b16 = (src + n + 15) & ~15
+    blo, bhi = max(a16, (lo + 15) & ~15), min(b16, hi & ~15)
+    return (blo, blo - a16, bhi - blo) if blo < bhi else (0, 0, 0)
+
+
+def check(BH, S, D, bs, half, occ, offs=(0, 0)):
+    elem = 2 if half else 1
+    RB = D * elem
+    LPR = RB // 16
+    G = WARPS * 32 // LPR
+    TILE = TILE_BYTES // RB
+    assert TILE == 4 * G
+    nsub = 1 if half else D // bs
+    slot = 0 if half else TILE * nsub * 2 + 32
+    qslot = D * 2 + 32
+    total = BH * S
+    grid, R, _ = make_plan(total, S, SMS * occ)
+    _, _, maxp = make_plan(total, S, SMS * BOUND_OCC)   # workspace layout bound
+    kbase, sbase, qbase = 1 << 40, (1 << 41) + offs[0], (1 << 42) + offs[1]
+    s_end, q_end = sbase + total * nsub * 2, qbase + BH * D * 2
+    covered = 0
+    for c in range(grid):
+        r0, r1 = c * R, min((c + 1) * R, total)
+        assert r0 < r1
+        r = r0
+        while r < r1:
+            bh = r // S
+            head0 = bh * S
+            ta, tb = r - head0, min(r1 - head0, S)
+            tiles = list(range(ta, tb, TILE))
+            # every tile of small cases; first/last few of big ones
+            if len(tiles) > 8:
+                tiles = tiles[:4] + tiles[-4:]
+            for t0 in tiles:
+                cnt = min(TILE, tb - t0)
+                row0 = head0 + t0
+                assert 0 < cnt <= TILE and row0 + cnt <= total
+                assert (kbase + row0 * RB) % 16 == 0 and cnt * RB % 16 == 0
+                assert cnt * RB <= TILE_BYTES
+                if not half:
+                    n = cnt * nsub * 2
+                    src = sbase + row0 * nsub * 2
+                    b_src, b_off, b_n = plan_span(src, n, sbase, s_end)
+                    if b_n:
+                        assert sbase <= b_src and b_src + b_n <= s_end
+                        assert b_src % 16 == 0 and b_n % 16 == 0 and b_off % 16 == 0
+                        assert b_off + b_n <= slot
+                    assert (src & 15) + 2 * TILE * nsub <= slot      # consumer reads
+                    a16 = src & ~15
+                    for p in range(src, src + n, 2):                 # edge plain loads
+                        if not (b_n and b_src <= p < b_src + b_n):
+                            assert sbase <= p < s_end and p - a16 + 2 <= slot
+                if t0 == ta:
+                    qsrc = qbase + bh * D * 2
+                    b_src, b_off, b_n = plan_span(qsrc, D * 2, qbase, q_end)
+                    if b_n:
+                        assert b_off + b_n <= qslot and qbase <= b_src and b_src + b_n <= q_end
+                    assert (qsrc & 15) + D * 2 <= qslot
+            c_first, c_last = head0 // R, (head0 + S - 1) // R
+            assert 0 <= c - c_first < c_last - c_first + 1 <= maxp
+            covered += tb - ta
+            r = head0 + tb
+    assert covered == total
+
+
+KINDS = [(64, 32, False), (64, 64, False), (128, 32, False), (128, 64, False), (128, 128, False),
+         (64, 64, True), (128, 128, True)]
+SHAPES = [(1, 1), (2, 7), (3, 63), (4, 65), (3, 129), (2, 1000), (2, 4097), (6, 300),
+          (1, 20000), (16, 2048), (96, 1024), (512, 8192), (128, 131072), (1, 1 << 20), (7, 999)]
+
+
+@pytest.mark.parametrize("D,bs,half", KINDS)
+@pytest.mark.parametrize("occ", [1, 4])
+def test_schedule_in_bounds(D, bs, half, occ):
+    for BH, S in SHAPES:
+        for offs in ((0, 0), (2, 14), (6, 2)):
+            check(BH, S, D, bs, half, occ, offs)
+
+
+def test_stage_layout_fits_four_ctas_per_sm():
+    """3-stage ring + merge scratch + barriers of the largest instantiation
+    (INT8, D = 128, bs = 32) leave room for four CTAs in 228 KB."""
+    RB, nsub = 128, 4
+    TILE = TILE_BYTES // RB
+    stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (128 * 2 + 32)
+    smem = STAGES * stage + WARPS * (128 + 2) * 4 + 2 * STAGES * 8 + 16
+    assert 4 * (smem + 1024) <= 228 * 1024, smem

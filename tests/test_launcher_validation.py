@@ -1,7 +1,7 @@
 """The reference-signature launchers reject exactly the shapes the reference
 rejects, with its message and std::abort() (reference src/kv_compress.cu:130-135,
-src/kv_reconstruct.cu:44-50, src/attention_baseline.cu:151-154,
-src/attention_int8_fused.cu:340-345, src/attention_int8_fused_online.cu:209-238).
+src/kv_reconstruct.cu:45-50, src/attention_baseline.cu:151-154,
+src/attention_int8_fused.cu:185-190, src/attention_int8_fused_online.cu:209-238).
 Validation happens before any CUDA call, so these run without a GPU, each in a
 child process (an abort ends the process)."""
 import os
