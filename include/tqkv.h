@@ -145,6 +145,43 @@ tqkv_status tqkv_lse_combine(const float* partials, void* o,
                              int R, int BH, int D, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* INT8 decode for callers that cannot allocate device memory.
+ * No counterpart in the reference.
+ *
+ * Who needs it: code that may not call cudaMalloc (or any allocator) on the
+ * path where it runs decode — an inference runtime whose memory planner owns
+ * every device buffer and forbids allocations inside an operator, a plugin
+ * host that hands a plugin its inputs and outputs but no allocator, or a thin
+ * FFI binding with no device allocator of its own.  tqkv_decode_int8 needs a
+ * caller-provided workspace for heads that are split across CTAs; this
+ * variant instead uses a fixed scratch array of TQKV_NOALLOC_SCRATCH_BYTES
+ * compiled into the library, present on every GPU that loads the library
+ * until the process exits.  The caller still provides q, K/V codes and
+ * scales, and O.  Same arguments, accepted set and results as
+ * tqkv_decode_int8, without the workspace pair.
+ *
+ * Limits and rules:
+ *   - shapes whose scratch (tqkv_decode_workspace_bytes) exceeds
+ *     TQKV_NOALLOC_SCRATCH_BYTES are refused with TQKV_ERR_WORKSPACE;
+ *   - the first call on a device looks up the array's device address (and
+ *     may load the library's device code); make that first call before any
+ *     stream capture;
+ *   - all calls on a device share the one array: calls that can overlap on
+ *     the GPU (different streams, or unordered host threads) race and must be
+ *     ordered by the caller.
+ * Nothing is allocated: no cudaMalloc/cudaFree and no allocating library
+ * routine; each call clears the array's ticket counters with a memset on
+ * `stream` before launching. */
+#define TQKV_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+
+tqkv_status tqkv_decode_int8_noalloc(const void* q,
+                                     const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs,
+                                     void* o,
+                                     int B, int H, int S, int D, int block_size,
+                                     cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Device-side failure flag.  Every wait inside the kernels is bounded; a wait
  * that runs out records a nonzero code here (and the kernel returns early)
  * instead of hanging the GPU.  Reads and clears the flag of the current

@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -490,3 +491,77 @@ tqkv_status tqkv_read_device_error(uint32_t* code_out) {
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// INT8 decode without any allocation: the split-S scratch is a fixed array in
+// this file's device memory instead of a caller-provided workspace.
+// ===========================================================================
+namespace tqkv {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = TQKV_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+
+// One copy per GPU that loads this library, alive until the process exits.
+// Host code must not pass this name to a kernel: on the host it is only a
+// stand-in; the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch, per device ordinal, looked up once.
+std::atomic<void*> g_noalloc_addr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+tqkv_status noalloc_scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e);
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return TQKV_ERR_UNSUPPORTED;
+    void* p = g_noalloc_addr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        p = g_noalloc_addr[dev].load(std::memory_order_relaxed);
+        if (p == nullptr) {
+            // with `dev` current: the address of this device's copy of the array
+            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess) return from_cuda(e);
+            g_noalloc_addr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
+    return TQKV_OK;
+}
+
+}  // namespace
+}  // namespace tqkv
+
+extern "C" tqkv_status tqkv_decode_int8_noalloc(const void* q, const int8_t* kq, const void* ks,
+                                                const int8_t* vq, const void* vs, void* o, int B,
+                                                int H, int S, int D, int block_size,
+                                                cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S < 0) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_fill_half(o, BH * D, 0x7e00u, stream);
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    // shapes whose split-S scratch does not fit the fixed array are refused
+    const size_t need = tqkv::decode_workspace_bytes(BH, S, D);
+    if (need > tqkv::kNoAllocScratchBytes) return TQKV_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    tqkv_status st = tqkv::noalloc_scratch_address(&scratch);
+    if (st != TQKV_OK) return st;
+    // The array keeps whatever the previous call left.  Only the ticket
+    // counters at its start must be zero when a launch begins (partial records
+    // are always written before they are read); a completed call leaves them
+    // zero, an interrupted one might not, so clear them every time.
+    const size_t ticket_bytes = (static_cast<size_t>(BH) * sizeof(unsigned int) + 255) / 256 * 256;
+    if (need > 0) {
+        st = tqkv::from_cuda(cudaMemsetAsync(scratch, 0, ticket_bytes, stream));
+        if (st != TQKV_OK) return st;
+    }
+    return tqkv::launch_decode(tqkv::KvKind::kInt8, tqkv::OutKind::kHalfO, q, kq, ks, vq, vs, o,
+                               static_cast<int>(BH), S, D, block_size, scratch,
+                               tqkv::kNoAllocScratchBytes, stream);
+}

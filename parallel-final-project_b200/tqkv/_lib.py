@@ -41,6 +41,8 @@ C_ABI = {
                                          c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "tqkv_lse_combine": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "tqkv_read_device_error": (c_int, [ctypes.POINTER(c_uint32)]),
+    "tqkv_decode_int8_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
 }
 
 # The reference's C++ launchers (include/attention.h, include/quantization.h),
