@@ -52,6 +52,13 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="int8_longctx")
+    p.add_argument("--shard", choices=["auto", "s", "bh"], default="auto",
+                   help="multi-GPU split: tokens (s, with NCCL all-gather) or heads (bh, no "
+                        "collective); auto = bh for int8_bh_shard, s otherwise")
+    p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="split-S record exchange: NVLink peer writes + bounded-wait combine "
+                        "(p2p), or NCCL all-gather + combine kernel (nccl, never graph-captured)")
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU baseline leg (rank 0, N=1)")
     p.add_argument("--cpu-budget-s", type=float, default=20.0,
@@ -253,17 +260,28 @@ def main():
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    # ---- inputs: this rank's token slice of every head ----
-    s0, s1 = W.token_slice(w.S, rank, world)
-    S_loc = s1 - s0
-    q = W.make_q(w, dev)
+    # ---- inputs: this rank's share of the workload ----
+    shard = args.shard if args.shard != "auto" else ("bh" if w.name == "int8_bh_shard" else "s")
+    if world == 1:
+        shard = "s"
+    BH, D = w.BH, w.D
+    if shard == "s":      # every head, tokens [s0, s1)
+        s0, s1 = W.token_slice(w.S, rank, world)
+        h0, h1 = 0, BH
+    else:                 # heads [h0, h1), every token; no collective
+        s0, s1 = 0, w.S
+        h0, h1 = W.head_slice(BH, rank, world)
+    S_loc, BH_loc = s1 - s0, h1 - h0
+    q = W.make_q(w, dev).reshape(1, BH, D)[:, h0:h1].contiguous()
     comp_us = []
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kvq = []
     for which in ("k", "v"):
-        x = W.make_kv_slice(w, which, s0, s1, dev)
+        x = W.make_kv_slice(w, which, s0, s1, dev).reshape(1, BH, S_loc, D)
+        if shard == "bh":
+            x = x[:, h0:h1].contiguous()
         xq = torch.empty(x.shape, dtype=torch.int8, device=dev)
-        xs = torch.empty(x.shape[:3] + (w.D // w.block_size,), dtype=torch.float16, device=dev)
+        xs = torch.empty(x.shape[:3] + (D // w.block_size,), dtype=torch.float16, device=dev)
         for rep in range(3):  # the first rep is warm-up; outputs are overwritten each rep
             ev0.record()
             tqkv.kv_compress(x, w.block_size, xq=xq, scales=xs)
@@ -275,30 +293,69 @@ def main():
         del x
         torch.cuda.empty_cache()
     (kq, ks), (vq, vs) = kvq
-    BH, D = w.BH, w.D
-    out = torch.empty((w.B, w.H, D), dtype=torch.float16, device=dev)
+    out = torch.empty((1, BH_loc, D), dtype=torch.float16, device=dev)
     ws = tqkv.Workspace(dev)
+    collective = world > 1 and shard == "s"
+    use_p2p = collective and args.exchange == "p2p"
     local_rec = torch.empty((BH, D + 2), dtype=torch.float32, device=dev)
     gathered = torch.empty((world, BH, D + 2), dtype=torch.float32, device=dev)
+    exchange = tqkv.PeerExchange(world, rank, BH, D) if use_p2p else None
 
-    def step(kernel_events=None):
-        if world == 1:
-            if kernel_events is not None:
-                kernel_events[0].record()
+    def kernel():
+        if use_p2p:
+            exchange.publish(q, kq, ks, vq, vs, w.block_size, workspace=ws)
+        elif collective:
+            tqkv.decode_int8_partial(q, kq, ks, vq, vs, w.block_size, out=local_rec, workspace=ws)
+        else:
             tqkv.decode_int8(q, kq, ks, vq, vs, w.block_size, out=out, workspace=ws)
-            if kernel_events is not None:
-                kernel_events[1].record()
-            return
-        if kernel_events is not None:
-            kernel_events[0].record()
-        tqkv.decode_int8_partial(q, kq, ks, vq, vs, w.block_size, out=local_rec, workspace=ws)
-        if kernel_events is not None:
-            kernel_events[1].record()
-        dist.all_gather_into_tensor(gathered, local_rec)
-        tqkv.lse_combine(gathered, D, out=out.view(BH, D))
 
+    def comm():
+        if use_p2p:
+            exchange.combine(out)
+        elif collective:
+            dist.all_gather_into_tensor(gathered, local_rec)
+            tqkv.lse_combine(gathered, D, out=out.view(BH, D))
+
+    q_host = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    q_host.copy_(q.cpu())
+    o_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        q.copy_(q_host, non_blocking=True)
+        kernel()
+        comm()
+        o_host.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 2)):   # also sets kernel attributes and the workspace
+        kernel()
+        comm()
+    torch.cuda.synchronize()
+
+    # CUDA graphs: one for the decode kernel, one for gather + combine, one for
+    # the whole end-to-end step; replays keep the GPU fed without launch gaps.
+    graphs = []
+    # NCCL collectives are never captured (capturing them hung here); the p2p
+    # exchange is two plain kernels and captures like the single-GPU step.
+    if not args.no_graph and not (collective and not use_p2p):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for fn in (kernel, comm, e2e_step):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        for fn in (kernel, comm, e2e_step):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            graphs.append(g)
+        run_kernel, run_comm, run_e2e = (g.replay for g in graphs)
+    else:
+        run_kernel, run_comm, run_e2e = kernel, comm, e2e_step
+    graphs_used = len(graphs) > 0
     for _ in range(args.warmup):
-        step()
+        run_kernel()
+        run_comm()
     torch.cuda.synchronize()
 
     # ---- timed region: exactly K steps ----
@@ -310,7 +367,10 @@ def main():
         torch.cuda.nvtx.range_push("tqkv_timed")  # lets ncu --nvtx-include select this region
         ev0.record()
         for i in range(args.steps):
-            step(kev[i])
+            kev[i][0].record()
+            run_kernel()
+            kev[i][1].record()
+            run_comm()
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -320,27 +380,21 @@ def main():
     err = tqkv.read_device_error()
 
     # ---- end to end through the public API: H2D q, decode, D2H O, per step ----
-    q_host = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
-    q_host.copy_(q.cpu())
-    o_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(3):
-        q.copy_(q_host, non_blocking=True)
-        step()
-        o_host.copy_(out, non_blocking=True)
+        run_e2e()
         torch.cuda.current_stream().synchronize()
     barrier()
     torch.cuda.synchronize()
     ev0.record()
     for _ in range(e2e_steps):
-        q.copy_(q_host, non_blocking=True)
-        step()
-        o_host.copy_(out, non_blocking=True)
+        run_e2e()
         torch.cuda.current_stream().synchronize()  # the next token needs O on the host
     ev1.record()
     torch.cuda.synchronize()
     barrier()
     e2e_ms_local = ev0.elapsed_time(ev1) / e2e_steps
+    del graphs, run_kernel, run_comm, run_e2e
 
     # ---- max over ranks ----
     t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, float(err)], device=dev)
@@ -349,7 +403,7 @@ def main():
     step_ms, kern_ms, e2e_ms, err_max = t.tolist()
 
     total_bytes = w.kv_bytes_int8()
-    local_bytes = w.kv_bytes_int8(S_loc)
+    local_bytes = w.kv_bytes_int8(S_loc) * BH_loc // BH
     peak, peak_kind = measured_peaks()
     value = total_bytes / (step_ms * 1e-3) / 1e9
     achieved = local_bytes / (kern_ms * 1e-3) / 1e9
@@ -364,6 +418,8 @@ def main():
         cpu = {"value": sample_bytes / cpu_t / 1e9, "unit": "GB/s", "cores": threads,
                "kind": "port", "sample": desc + f"; median of 5 runs, {cpu_t * 1e3:.1f} ms each"}
 
+    if exchange is not None:
+        exchange.close()
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -386,11 +442,14 @@ def main():
         "config": {
             "workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D,
             "block_size": w.block_size, "global_batch": w.B, "seq_len": w.S,
-            "parallelism": f"split-S x{world}" if world > 1 else "1 GPU",
+            "parallelism": (f"split-S x{world} + NVLink peer exchange" if use_p2p else
+                            f"split-S x{world} + NCCL all-gather" if collective else
+                            f"B*H shards x{world}, no collective" if world > 1 else "1 GPU"),
+            "cuda_graphs": bool(graphs_used),
             "l2": f"inputs {total_bytes / 1e9:.2f} GB per step > 126 MB L2; no flush needed",
         },
         "roofline": {
-            "bound": "hbm", "kernel": DECODE_KERNEL if world == 1 else DECODE_KERNEL + " (partial)",
+            "bound": "hbm", "kernel": DECODE_KERNEL + (" (split-S partial)" if collective else ""),
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": peak_kind, "traffic": traffic,
             "algorithmic_bytes_per_launch": local_bytes, "launch_ms": kern_ms,
@@ -400,7 +459,7 @@ def main():
                 "us_per_step": e2e_ms * 1e3,
                 "h2d_bytes_per_step": q.numel() * q.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
-        "gpu_launches": args.steps * (1 if world == 1 else 2),
+        "gpu_launches": args.steps * (2 if collective else 1),
         "clocks": clk.summary(),
         "compress": {"us_per_tensor": statistics.mean(comp_us),
                      "GBps": (w.BH * S_loc * w.D * 3 + w.BH * S_loc * (w.D // w.block_size) * 2)

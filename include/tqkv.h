@@ -145,6 +145,46 @@ tqkv_status tqkv_lse_combine(const float* partials, void* o,
                              int R, int BH, int D, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Split-S decode across the GPUs of one node over NVLink, without NCCL (no
+ * counterpart in the reference, which has no multi-GPU path).
+ *
+ * Every rank allocates one exchange buffer (tqkv_exchange_alloc, size
+ * tqkv_exchange_bytes(world, B*H, D)), exports it with tqkv_ipc_get_handle,
+ * and maps every other rank's buffer with tqkv_ipc_open_handle (plain CUDA
+ * IPC peer mappings; no multicast objects).  `exchange_bufs[r]` is rank r's
+ * buffer as mapped in the calling process.  Per decode step, on each rank's
+ * stream:
+ *   tqkv_decode_int8_publish  computes this rank's per-head records
+ *       (acc[D], m, l) over its token slice and stores them into every rank's
+ *       buffer through the peer mappings; each value travels with the step
+ *       number in one 64-bit store, so no fence or flag is needed;
+ *   tqkv_exchange_combine     waits (bounded, ~1 s) until every rank's
+ *       entries of this step have arrived in this rank's buffer, merges them
+ *       into O and advances this rank's step counter.
+ * Steps alternate between two record slots, so a rank can run one step ahead
+ * of another without overwriting records still being read.  Buffers must be
+ * zero when first used (tqkv_exchange_alloc zeroes them) and stay in use for
+ * the whole sequence of steps.  An entry that never arrives sets the device
+ * error flag (tqkv_read_device_error) instead of hanging.  world <= 8. */
+size_t tqkv_exchange_bytes(int world, int BH, int D);
+tqkv_status tqkv_exchange_alloc(size_t bytes, void** buf_out);
+tqkv_status tqkv_exchange_free(void* buf);
+/* 64-byte CUDA IPC handle of an exchange buffer, and its mapping in another process. */
+tqkv_status tqkv_ipc_get_handle(const void* buf, void* handle_out);
+tqkv_status tqkv_ipc_open_handle(const void* handle, void** buf_out);
+tqkv_status tqkv_ipc_close_handle(void* buf);
+
+tqkv_status tqkv_decode_int8_publish(const void* q,
+                                     const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs,
+                                     int B, int H, int S, int D, int block_size,
+                                     void* workspace, size_t workspace_bytes,
+                                     void* const* exchange_bufs, int world, int rank,
+                                     cudaStream_t stream);
+tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o,
+                                  int world, int rank, int BH, int D, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* INT8 decode for callers that cannot allocate device memory.
  * No counterpart in the reference.
  *

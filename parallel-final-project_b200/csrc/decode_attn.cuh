@@ -62,8 +62,43 @@ constexpr int kMergeBarrier = 1;        // named barrier id used by consumers
 enum DecodeOut : int {
     kOutHalf = 0,     // write O (fp16)
     kOutPartial = 1,  // write per-head (acc[D], m, l) records, natural-log units
+    kOutPeers = 2,    // write the records into every rank's exchange buffer, then
+                      // raise this rank's step flag on every rank (split-S over NVLink)
 };
 
+// Exchange buffer of one rank (split-S across the GPUs of a node), written by
+// every rank through CUDA IPC peer mappings (no multicast).  Each value
+// travels with its step number in one naturally aligned 64-bit store
+// ({float bits, step}), so a reader knows a value has arrived when its step
+// matches: no fences or flags sit between the producer and the consumer.
+//   header (512 B): step   at +128   steps this rank has completed (combined)
+//                   done   at +256   combine CTAs finished in the current step
+//   records:        uint64 [2][world][BH][D + 2]   slot = step parity; entry
+//                   (slot, r, bh) holds rank r's (acc[0..D-1], m, l) of head bh
+constexpr int kMaxPeers = 8;
+constexpr int kHdrEpoch = 32;     // in uint32 units
+constexpr int kHdrDone = 64;
+constexpr int kExchangeHeaderBytes = 512;
+
+struct PeerArgs {
+    unsigned long long* recs[kMaxPeers];  // records area of each rank's buffer
+    unsigned int* own;                    // this rank's header
+    unsigned long long* own_recs;         // this rank's records area
+    int world;
+    int rank;
+};
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long pack_step(float v, unsigned int step) {
+    return (static_cast<unsigned long long>(step) << 32) | __float_as_uint(v);
+}
 struct DecodeArgs {
     const void* q;             // fp16 [BH][D]
     const void* k;             // int8 or fp16 [BH][S][D]
@@ -79,6 +114,7 @@ struct DecodeArgs {
     int BH;
     int max_parts;
     float score_scale_log2;    // log2(e) / sqrt(D)
+    PeerArgs peer;             // kOutPeers only
 };
 
 template <int D, int BS, bool kHalfKV>
@@ -549,13 +585,61 @@ __device__ __forceinline__ void lse_factors(float m, float mo, float& M, float& 
     fb = fast_exp2(mo - base);
 }
 
+// Write a finished head: O (fp16), a partial record, or the record in every
+// rank's exchange buffer followed, for the step's last head, by the step flag.
+// All consumer threads call it; A is this thread's dim (tid < D); M2 is in
+// base-2 units.
+template <int D, int OUT>
+__device__ __forceinline__ void emit_head(const DecodeArgs& a, int bh, int tid, float A, float M2,
+                                          float L) {
+    constexpr float kLn2 = 0.69314718055994530942f;
+    if constexpr (OUT == kOutHalf) {
+        if (tid < D)
+            static_cast<__half*>(a.out)[static_cast<long long>(bh) * D + tid] =
+                __float2half_rn(A * (1.0f / L));
+    } else if constexpr (OUT == kOutPartial) {
+        if (tid < D) {
+            float* rec = static_cast<float*>(a.out) + static_cast<long long>(bh) * (D + 2);
+            rec[tid] = A;
+            if (tid == 0) {
+                rec[D] = M2 * kLn2;
+                rec[D + 1] = L;
+            }
+        }
+    } else {
+        // every rank's buffer gets this head's record, each value stored
+        // together with the step number (see the exchange buffer layout)
+        const unsigned int step = __ldcg(a.peer.own + kHdrEpoch) + 1u;
+        const long long off =
+            ((static_cast<long long>(step & 1u) * a.peer.world + a.peer.rank) * a.BH + bh) *
+            (D + 2);
+        if (tid < D) {
+            const unsigned long long va = pack_step(A, step);
+            const unsigned long long vm = pack_step(M2 * kLn2, step);
+            const unsigned long long vl = pack_step(L, step);
+#pragma unroll
+            for (int p = 0; p < kMaxPeers; ++p) {
+                if (p < a.peer.world) {
+                    unsigned long long* rec = a.peer.recs[p] + off;
+                    st_volatile_u64(rec + tid, va);
+                    if (tid == 0) {
+                        st_volatile_u64(rec + D, vm);
+                        st_volatile_u64(rec + D + 1, vl);
+                    }
+                }
+            }
+        }
+    }
+}
+
 // Finish one segment: merge the lane-group states of the CTA, then either
 // write O / the partial record (head owned by this CTA alone), or publish a
 // partial and let the last CTA of the head merge all of them.
 template <int D, int BS, bool kHalfKV, int OUT>
-__device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, const DecodeArgs& a,
-                                               float* merge, int* flag, int bh, int part,
-                                               int nparts, int tid) {
+__device__ __forceinline__ unsigned int finish_segment(SegState<D, BS, kHalfKV>& st,
+                                                       const DecodeArgs& a, float* merge,
+                                                       int* flag, int bh, int part, int nparts,
+                                                       int tid) {
     using C = DecodeCfg<D, BS, kHalfKV>;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -614,23 +698,10 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
         }
     }
 
-    constexpr float kLn2 = 0.69314718055994530942f;
     if (nparts == 1) {
-        if (tid < D) {
-            if constexpr (OUT == kOutHalf) {
-                static_cast<__half*>(a.out)[static_cast<long long>(bh) * D + tid] =
-                    __float2half_rn(A * (1.0f / L));
-            } else {
-                float* rec = static_cast<float*>(a.out) + static_cast<long long>(bh) * (D + 2);
-                rec[tid] = A;
-                if (tid == 0) {
-                    rec[D] = M * kLn2;
-                    rec[D + 1] = L;
-                }
-            }
-        }
+        emit_head<D, OUT>(a, bh, tid, A, M, L);
         named_barrier_sync(kMergeBarrier, kDecodeConsumers);  // merge[] reused next segment
-        return;
+        return 1u;
     }
 
     // publish this CTA's piece of the head
@@ -652,28 +723,17 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
     if (*flag) {
         __threadfence();
         const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
+        float Mt = -INFINITY, At = 0.0f, Lt = 0.0f;
         if (tid < D) {
-            float Mt = -INFINITY;
             for (int p = 0; p < nparts; ++p) Mt = fmaxf(Mt, __ldcg(recs + p * (D + 2) + D));
             const float base = Mt == -INFINITY ? 0.0f : Mt;
-            float At = 0.0f, Lt = 0.0f;
             for (int p = 0; p < nparts; ++p) {
                 const float f = fast_exp2(__ldcg(recs + p * (D + 2) + D) - base);
                 Lt = fmaf(__ldcg(recs + p * (D + 2) + D + 1), f, Lt);
                 At = fmaf(__ldcg(recs + p * (D + 2) + tid), f, At);
             }
-            if constexpr (OUT == kOutHalf) {
-                static_cast<__half*>(a.out)[static_cast<long long>(bh) * D + tid] =
-                    __float2half_rn(At * (1.0f / Lt));
-            } else {
-                float* rec = static_cast<float*>(a.out) + static_cast<long long>(bh) * (D + 2);
-                rec[tid] = At;
-                if (tid == 0) {
-                    rec[D] = Mt * kLn2;
-                    rec[D + 1] = Lt;
-                }
-            }
         }
+        emit_head<D, OUT>(a, bh, tid, At, Mt, Lt);
         // leave the workspace all-zero for the next call, whatever its shape:
         // the ticket, and every record this merge consumed
         named_barrier_sync(kMergeBarrier, kDecodeConsumers);
@@ -682,6 +742,7 @@ __device__ __forceinline__ void finish_segment(SegState<D, BS, kHalfKV>& st, con
         if (tid == 0) a.tickets[bh] = 0u;
     }
     named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+    return *flag ? 1u : 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -727,6 +788,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     // A warp whose bounded wait ran out stops computing but keeps walking the
     // schedule, so that the consumer-wide named barriers still see every warp.
     bool broken = false;
+    unsigned int emitted = 0;  // heads this CTA finished (kOutPeers bookkeeping)
 
     for (long long rr = r0; rr < r1;) {
         const int bh = static_cast<int>(rr / a.S);
@@ -773,9 +835,10 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         const long long c_last = (head0 + a.S - 1) / a.rows_per_cta;
         const int nparts = static_cast<int>(c_last - c_first + 1);
         const int part = static_cast<int>(blockIdx.x - c_first);
-        finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, flag, bh, part, nparts, tid);
+        emitted += finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, flag, bh, part, nparts, tid);
         rr = head0 + t_b;
     }
+    (void)emitted;
 }
 
 // Log-sum-exp merge of R partial records per head (natural-log units):
@@ -797,6 +860,90 @@ __global__ void __launch_bounds__(D)
         A = fmaf(rec[r * stride + t], f, A);
     }
     o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
+}
+
+// Split-S step over NVLink, second half: wait (bounded) until every rank has
+// published the current step into this rank's exchange buffer, then merge the
+// world records of each head (natural-log units) into O.  One CTA per head.
+template <int D>
+__global__ void __launch_bounds__(D)
+    exchange_combine_kernel(const PeerArgs p, __half* __restrict__ o, int BH) {
+    const int bh = blockIdx.x;
+    const int t = threadIdx.x;
+    const unsigned int step = __ldcg(p.own + kHdrEpoch) + 1u;
+    const long long stride = static_cast<long long>(BH) * (D + 2);
+    const unsigned long long* rec =
+        p.own_recs + (static_cast<long long>(step & 1u) * p.world * BH + bh) * (D + 2);
+    // Issue every load of this thread's 3 * world entries at once (one round
+    // trip when the peers are done, the usual case), then re-poll only while
+    // some entry still carries an older step.
+    unsigned long long v[3 * kMaxPeers];
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            v[3 * r] = ld_volatile_u64(rec + r * stride + D);
+            v[3 * r + 1] = ld_volatile_u64(rec + r * stride + D + 1);
+            v[3 * r + 2] = ld_volatile_u64(rec + r * stride + t);
+        }
+    }
+    bool ready = true;
+#pragma unroll
+    for (int i = 0; i < 3 * kMaxPeers; ++i)
+        if (i < 3 * p.world) ready = ready && static_cast<unsigned int>(v[i] >> 32) == step;
+    if (!ready) {
+        const long long start = clock64();
+#pragma unroll 1
+        for (uint32_t it = 0; it < (1u << 30) && !ready; ++it) {
+            ready = true;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r < p.world) {
+                    const unsigned long long* base = rec + r * stride;
+                    if (static_cast<unsigned int>(v[3 * r] >> 32) != step) v[3 * r] = ld_volatile_u64(base + D);
+                    if (static_cast<unsigned int>(v[3 * r + 1] >> 32) != step) v[3 * r + 1] = ld_volatile_u64(base + D + 1);
+                    if (static_cast<unsigned int>(v[3 * r + 2] >> 32) != step) v[3 * r + 2] = ld_volatile_u64(base + t);
+                    ready = ready && static_cast<unsigned int>(v[3 * r] >> 32) == step &&
+                            static_cast<unsigned int>(v[3 * r + 1] >> 32) == step &&
+                            static_cast<unsigned int>(v[3 * r + 2] >> 32) == step;
+                }
+            }
+            if (clock64() - start > (1ll << 31)) break;
+        }
+        if (!ready) record_device_error(kErrPeerWaitTimeout);
+    }
+    float m[kMaxPeers], l[kMaxPeers], acc[kMaxPeers];
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            m[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r]));
+            l[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r + 1]));
+            acc[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r + 2]));
+            M = fmaxf(M, m[r]);
+        }
+    }
+    const float base = M == -INFINITY ? 0.0f : M;
+    float A = 0.0f, L = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            const float f = __expf(m[r] - base);
+            L = fmaf(l[r], f, L);
+            A = fmaf(acc[r], f, A);
+        }
+    }
+    o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
+    // the last CTA of the step advances this rank's step counter; every CTA
+    // has read it above, before adding itself to the count
+    __syncthreads();
+    if (t == 0) {
+        __threadfence();
+        const unsigned int prev = atomicAdd(p.own + kHdrDone, 1u);
+        if (prev == static_cast<unsigned int>(BH - 1)) {
+            p.own[kHdrDone] = 0u;
+            p.own[kHdrEpoch] = step;
+        }
+    }
 }
 
 // Fill `n` fp16 values with `bits` (used for S == 0 outputs).

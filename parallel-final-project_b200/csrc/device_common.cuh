@@ -20,6 +20,7 @@ enum DeviceErrorCode : unsigned int {
     kErrFullWaitTimeout = 1,     // consumer waited too long for a tile
     kErrEmptyWaitTimeout = 2,    // producer waited too long for a free stage
     kErrDrainTimeout = 3,        // producer's copies never completed
+    kErrPeerWaitTimeout = 4,     // a peer GPU's exchange flag never arrived
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {
@@ -100,6 +101,31 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// System-scope release store / acquire load of a 32-bit flag (peer GPUs
+// read and write these through NVLink peer mappings).
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until *flag (a step counter) reaches `target`, with the same hard
+// bound as mbar_wait_bounded.  Wrap-safe comparison.
+__device__ __forceinline__ bool wait_flag_bounded(const unsigned int* flag, unsigned int target) {
+    if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
+    const long long start = clock64();
+#pragma unroll 1
+    for (uint32_t it = 0; it < (1u << 30); ++it) {
+        if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
+        if (clock64() - start > (1ll << 31)) break;
+        __nanosleep(64);
+    }
+    return false;
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.

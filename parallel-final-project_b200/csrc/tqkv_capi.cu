@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -186,6 +187,7 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
 template <int D, int BS, bool kHalfKV, int OUT>
 tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void* workspace,
                         size_t workspace_bytes, cudaStream_t stream) {
+    // a.peer is set by the caller (kOutPeers) or zero
     using C = DecodeCfg<D, BS, kHalfKV>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -220,7 +222,55 @@ tqkv_status decode_out(OutKind out, const DecodeArgs& a, long long total, int S,
                        void* ws, size_t wsb, cudaStream_t stream) {
     if (out == OutKind::kHalfO)
         return decode_impl<D, BS, kHalfKV, kOutHalf>(a, total, S, BH, ws, wsb, stream);
-    return decode_impl<D, BS, kHalfKV, kOutPartial>(a, total, S, BH, ws, wsb, stream);
+    if (out == OutKind::kPartial)
+        return decode_impl<D, BS, kHalfKV, kOutPartial>(a, total, S, BH, ws, wsb, stream);
+    if constexpr (!kHalfKV)
+        return decode_impl<D, BS, kHalfKV, kOutPeers>(a, total, S, BH, ws, wsb, stream);
+    return TQKV_ERR_UNSUPPORTED;
+}
+
+// INT8 decode with the kOutPeers epilogue (split-S over NVLink).
+tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void* k, const void* ks,
+                                const void* v, const void* vs, int BH, int S, int D, int bs,
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.ks = static_cast<const uint16_t*>(ks);
+    a.vs = static_cast<const uint16_t*>(vs);
+    a.out = nullptr;
+    a.peer = peer;
+    const long long total = static_cast<long long>(BH) * S;
+    const OutKind o = OutKind::kPeers;
+    if (D == 64 && bs == 32) return decode_out<64, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 64 && bs == 64) return decode_out<64, 64, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 32) return decode_out<128, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 64) return decode_out<128, 64, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 128) return decode_out<128, 128, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    return TQKV_ERR_UNSUPPORTED;
+}
+
+size_t exchange_bytes(int world, long long BH, int D) {
+    return kExchangeHeaderBytes +
+           align_up(static_cast<size_t>(2) * world * BH * (D + 2) * sizeof(unsigned long long),
+                    256);
+}
+
+// PeerArgs from the host array of every rank's exchange buffer.
+tqkv_status make_peer_args(void* const* bufs, int world, int rank, PeerArgs* out) {
+    PeerArgs peer{};
+    for (int r = 0; r < world; ++r) {
+        if (!bufs[r]) return TQKV_ERR_NULL;
+        uint8_t* base = static_cast<uint8_t*>(bufs[r]);
+        peer.recs[r] = reinterpret_cast<unsigned long long*>(base + kExchangeHeaderBytes);
+    }
+    peer.own = static_cast<unsigned int*>(bufs[rank]);
+    peer.own_recs = peer.recs[rank];
+    peer.world = world;
+    peer.rank = rank;
+    *out = peer;
+    return TQKV_OK;
 }
 
 template <int D>
@@ -488,6 +538,99 @@ tqkv_status tqkv_read_device_error(uint32_t* code_out) {
     if (e != cudaSuccess) return tqkv::from_cuda(e);
     *code_out = v;
     return TQKV_OK;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Split-S across the GPUs of one node over NVLink peer mappings (no NCCL)
+// ===========================================================================
+extern "C" {
+
+size_t tqkv_exchange_bytes(int world, int BH, int D) {
+    if (world <= 0 || world > tqkv::kMaxPeers || BH <= 0 || (D != 64 && D != 128)) return 0;
+    return tqkv::exchange_bytes(world, BH, D);
+}
+
+tqkv_status tqkv_exchange_alloc(size_t bytes, void** buf_out) {
+    if (!buf_out || bytes == 0) return TQKV_ERR_NULL;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);  // a whole allocation: its IPC handle maps exactly it
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return tqkv::from_cuda(e);
+    }
+    *buf_out = p;
+    return TQKV_OK;
+}
+
+tqkv_status tqkv_exchange_free(void* buf) {
+    if (!buf) return TQKV_OK;
+    return tqkv::from_cuda(cudaFree(buf));
+}
+
+tqkv_status tqkv_ipc_get_handle(const void* buf, void* handle_out) {
+    if (!buf || !handle_out) return TQKV_ERR_NULL;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(buf));
+    if (e != cudaSuccess) return tqkv::from_cuda(e);
+    std::memcpy(handle_out, &h, sizeof(h));
+    return TQKV_OK;
+}
+
+tqkv_status tqkv_ipc_open_handle(const void* handle, void** buf_out) {
+    if (!handle || !buf_out) return TQKV_ERR_NULL;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return tqkv::from_cuda(e);
+    *buf_out = p;
+    return TQKV_OK;
+}
+
+tqkv_status tqkv_ipc_close_handle(void* buf) {
+    if (!buf) return TQKV_OK;
+    return tqkv::from_cuda(cudaIpcCloseMemHandle(buf));
+}
+
+tqkv_status tqkv_decode_int8_publish(const void* q, const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs, int B, int H, int S, int D,
+                                     int block_size, void* workspace, size_t workspace_bytes,
+                                     void* const* exchange_bufs, int world, int rank,
+                                     cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S <= 0 || world <= 0 || world > tqkv::kMaxPeers || rank < 0 ||
+        rank >= world)
+        return TQKV_ERR_INVALID_SIZE;
+    if (!q || !kq || !ks || !vq || !vs || !exchange_bufs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    tqkv::PeerArgs peer{};
+    const tqkv_status pst = tqkv::make_peer_args(exchange_bufs, world, rank, &peer);
+    if (pst != TQKV_OK) return pst;
+    return tqkv::launch_decode_peers(peer, q, kq, ks, vq, vs, static_cast<int>(BH), S, D,
+                                     block_size, workspace, workspace_bytes, stream);
+}
+
+tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o, int world, int rank,
+                                  int BH, int D, cudaStream_t stream) {
+    if (D != 64 && D != 128) return TQKV_ERR_UNSUPPORTED;
+    if (world <= 0 || world > tqkv::kMaxPeers || rank < 0 || rank >= world || BH <= 0)
+        return TQKV_ERR_INVALID_SIZE;
+    if (!exchange_bufs || !o) return TQKV_ERR_NULL;
+    tqkv::PeerArgs peer{};
+    const tqkv_status pst = tqkv::make_peer_args(exchange_bufs, world, rank, &peer);
+    if (pst != TQKV_OK) return pst;
+    if (D == 64)
+        return tqkv::from_cuda(tqkv::launch_kernel(tqkv::exchange_combine_kernel<64>, dim3(BH),
+                                                   dim3(64), 0, stream, peer,
+                                                   static_cast<__half*>(o), BH));
+    return tqkv::from_cuda(tqkv::launch_kernel(tqkv::exchange_combine_kernel<128>, dim3(BH),
+                                               dim3(128), 0, stream, peer,
+                                               static_cast<__half*>(o), BH));
 }
 
 }  // extern "C"

@@ -11,7 +11,7 @@
 namespace tqkv {
 
 enum class KvKind : int { kInt8 = 0, kHalf = 1 };
-enum class OutKind : int { kHalfO = 0, kPartial = 1 };
+enum class OutKind : int { kHalfO = 0, kPartial = 1, kPeers = 2 };
 
 // Records `err` as this host thread's last CUDA error and returns
 // TQKV_ERR_CUDA, or returns TQKV_OK for cudaSuccess.

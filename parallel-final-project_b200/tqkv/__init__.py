@@ -8,9 +8,10 @@ benchmark workloads, and orchestrates multi-GPU decode.
 from ._lib import LIB_PATH, TqkvError, load
 from .ops import (Workspace, decode_fp16, decode_int8, decode_int8_partial, kv_compress,
                   kv_reconstruct, lse_combine, read_device_error, workspace_bytes)
+from .peer import LocalExchange, PeerExchange
 
 __all__ = [
     "LIB_PATH", "TqkvError", "load", "Workspace", "decode_fp16", "decode_int8",
     "decode_int8_partial", "kv_compress", "kv_reconstruct", "lse_combine",
-    "read_device_error", "workspace_bytes",
+    "read_device_error", "workspace_bytes", "PeerExchange", "LocalExchange",
 ]

@@ -1,0 +1,111 @@
+"""Split-S decode across the GPUs of one node over NVLink peer mappings.
+
+Each rank owns one exchange buffer (flags, step counter and double-buffered
+per-head records, see include/tqkv.h).  The buffers are shared with CUDA IPC
+handles, exchanged once through torch.distributed, so every rank can read
+every other rank's records and raise its step flag in every buffer.  Per
+decode step:
+
+    publish(...)   decode kernel over this rank's token slice; its records go
+                   to its own buffer and its step flag to every buffer
+    combine(out)   bounded wait for every rank's flag, then every rank's
+                   records are read over NVLink and merged into O
+
+Both are plain kernel launches on the caller's stream, so a step can be
+captured in a CUDA graph.  No NCCL call and no multicast object is involved.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from ._lib import check, load
+from .ops import Workspace, _stream_handle, _workspace, workspace_bytes
+
+
+class PeerExchange:
+    def __init__(self, world: int, rank: int, BH: int, D: int, group=None):
+        lib = load()
+        self.world, self.rank, self.BH, self.D = world, rank, BH, D
+        self.group = group
+        nbytes = int(lib.tqkv_exchange_bytes(world, BH, D))
+        if nbytes == 0:
+            raise ValueError(f"unsupported exchange shape world={world} BH={BH} D={D}")
+        own = ctypes.c_void_p()
+        check("tqkv_exchange_alloc", lib.tqkv_exchange_alloc(nbytes, ctypes.byref(own)))
+        self.own = own.value
+        handle = (ctypes.c_ubyte * 64)()
+        check("tqkv_ipc_get_handle", lib.tqkv_ipc_get_handle(self.own, handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs, self._opened = [], []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self.own)
+                continue
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r])
+            p = ctypes.c_void_p()
+            check("tqkv_ipc_open_handle", lib.tqkv_ipc_open_handle(h, ctypes.byref(p)))
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        self.bufs = (ctypes.c_void_p * world)(*ptrs)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every buffer is zeroed and mapped before the first step
+
+    def publish(self, q, kq, ks, vq, vs, block_size: int, workspace: Optional[Workspace] = None,
+                stream=None) -> None:
+        B, H, S, D = kq.shape
+        ws = _workspace(workspace, q.device)
+        wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
+        check("tqkv_decode_int8_publish", load().tqkv_decode_int8_publish(
+            q.data_ptr(), kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
+            B, H, S, D, block_size, wptr, wbytes, self.bufs, self.world, self.rank,
+            _stream_handle(stream)))
+
+    def combine(self, out: torch.Tensor, stream=None) -> torch.Tensor:
+        check("tqkv_exchange_combine", load().tqkv_exchange_combine(
+            self.bufs, out.data_ptr(), self.world, self.rank, self.BH, self.D,
+            _stream_handle(stream)))
+        return out
+
+    def close(self) -> None:
+        """Unmap and free, once no rank can still write into any buffer."""
+        if self.own is None:
+            return
+        lib = load()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            check("tqkv_ipc_close_handle", lib.tqkv_ipc_close_handle(p))
+        self._opened = []
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # nobody still holds a mapping of our buffer
+        check("tqkv_exchange_free", lib.tqkv_exchange_free(self.own))
+        self.own = None
+
+
+class LocalExchange:
+    """The same two-launch step with a single rank (world = 1), on one GPU:
+    the combine waits only for this rank's own flag, which the publish launch
+    before it on the same stream has raised."""
+
+    def __init__(self, BH: int, D: int):
+        lib = load()
+        self.world, self.rank, self.BH, self.D = 1, 0, BH, D
+        nbytes = int(lib.tqkv_exchange_bytes(1, BH, D))
+        own = ctypes.c_void_p()
+        check("tqkv_exchange_alloc", lib.tqkv_exchange_alloc(nbytes, ctypes.byref(own)))
+        self.own = own.value
+        self.bufs = (ctypes.c_void_p * 1)(self.own)
+
+    publish = PeerExchange.publish
+    combine = PeerExchange.combine
+
+    def close(self) -> None:
+        if self.own is not None:
+            torch.cuda.synchronize()
+            check("tqkv_exchange_free", load().tqkv_exchange_free(self.own))
+            self.own = None

@@ -285,3 +285,25 @@ def test_decode_vs_reference_kernels_golden(name):
         ref = np.asarray(bits, np.uint16).view(np.float16).astype(np.float64)
         assert max_abs(got, ref) < REF_TOL
         assert_tight(got, ref)
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (64, 32)])
+def test_exchange_publish_combine_single_rank(D, bs):
+    """The NVLink exchange path with one rank on one GPU: publish (records +
+    step flag) then combine, for several consecutive steps (both record slots,
+    changing q), equals the plain decode."""
+    B, H, S = 2, 5, 9000
+    k, v = _rand((B, H, S, D), 51), _rand((B, H, S, D), 52)
+    kq, ks, vq, vs = _compress_kv(k, v, bs)
+    ex = tqkv.LocalExchange(B * H, D)
+    try:
+        for step in range(5):
+            q = _rand((B, H, D), 60 + step)
+            ex.publish(q, kq, ks, vq, vs, bs)
+            o = ex.combine(torch.empty((B, H, D), dtype=torch.float16, device="cuda"))
+            ref = tqkv.decode_int8(q, kq, ks, vq, vs, bs)
+            torch.cuda.synchronize()
+            assert max_abs(to_np(o), to_np(ref)) < 1e-3, step
+        assert tqkv.read_device_error() == 0
+    finally:
+        ex.close()

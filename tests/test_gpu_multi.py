@@ -1,7 +1,8 @@
 """Split-S decode across GPUs: each rank holds a token slice of every head,
 runs the partial kernel, the records are all-gathered over NCCL and merged by
-the LSE combine kernel on every rank.  The result must equal the one-GPU
-decode of the whole sequence.  Runs as one child process per GPU (2 to 4
+the LSE combine kernel on every rank; and the same split over NVLink peer
+mappings (publish + combine, no NCCL) for several consecutive steps.  Both
+must equal the one-GPU decode of the whole sequence.  Runs as one child process per GPU (2 to 4
 GPUs, NCCL with NVLS off); skipped when fewer than 2 GPUs are visible."""
 import datetime
 import os
@@ -52,6 +53,18 @@ def _rank_main(rank, world, port, q_out):
         full = tqkv.decode_int8(q, kqf, ksf, vqf, vsf, w.block_size)
         torch.cuda.synchronize()
         err = (o.float() - full.float()).abs().max().item()
+        # the same split over NVLink peer mappings (no NCCL), several steps
+        ex = tqkv.PeerExchange(world, rank, w.BH, w.D)
+        try:
+            for step in range(4):
+                qs = (q.float() * (1.0 + 0.25 * step)).half()
+                ex.publish(qs, kq, ks, vq, vs, w.block_size)
+                o2 = ex.combine(torch.empty_like(o))
+                ref2 = tqkv.decode_int8(qs, kqf, ksf, vqf, vsf, w.block_size)
+                torch.cuda.synchronize()
+                err = max(err, (o2.float() - ref2.float()).abs().max().item())
+        finally:
+            ex.close()
         q_out.put((rank, err, tqkv.read_device_error()))
     finally:
         dist.destroy_process_group()
