@@ -83,6 +83,17 @@ tqkv_status tqkv_kv_reconstruct(const int8_t* xq, const void* scales, void* y,
                                 int B, int H, int S, int D, int block_size,
                                 cudaStream_t stream);
 
+/* Incremental append (the step before attention in a decoder; no counterpart
+ * in the reference, whose compress takes whole tensors).  Quantises T new
+ * tokens per head, x = fp16 [B, H, T, D], into rows [t0, t0 + T) of an INT8
+ * cache with room for S_cap rows per head: cache_q int8 [B, H, S_cap, D],
+ * cache_s fp16 [B, H, S_cap, D / block_size].  Codes and scales are those
+ * tqkv_kv_compress gives for the same rows (same rule, same division).
+ * Requires 0 <= t0 and t0 + T <= S_cap; x and cache_q 16-byte aligned. */
+tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
+                           int B, int H, int T, int D, int block_size,
+                           int S_cap, int t0, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Decode attention: O[b,h,:] = softmax(q . K^T / sqrt(D)) . V per (b, h).
  *
@@ -112,6 +123,18 @@ tqkv_status tqkv_decode_int8(const void* q,
                              int B, int H, int S, int D, int block_size,
                              void* workspace, size_t workspace_bytes,
                              cudaStream_t stream);
+
+/* tqkv_decode_int8 over the first S rows of each head of caches that hold
+ * S_cap >= S rows per head (the layout tqkv_kv_append fills):
+ * kq/vq int8 [B, H, S_cap, D], ks/vs fp16 [B, H, S_cap, D / block_size].
+ * Workspace as for tqkv_decode_int8 with the same B, H, S, D. */
+tqkv_status tqkv_decode_int8_cache(const void* q,
+                                   const int8_t* kq, const void* ks,
+                                   const int8_t* vq, const void* vs,
+                                   void* o,
+                                   int B, int H, int S, int S_cap, int D, int block_size,
+                                   void* workspace, size_t workspace_bytes,
+                                   cudaStream_t stream);
 
 /* FP16 decode attention on the same split-S skeleton.
  * Replaces launch_decode_attn_baseline (reference include/attention.h:6-12,

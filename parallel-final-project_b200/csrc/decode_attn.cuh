@@ -110,7 +110,8 @@ struct DecodeArgs {
     unsigned int* tickets;     // workspace [BH]
     long long total_rows;      // BH * S
     long long rows_per_cta;    // R
-    int S;
+    int S;                     // rows attended per head
+    int S_stride;              // rows between consecutive heads in K/V/scales (>= S)
     int BH;
     int max_parts;
     float score_scale_log2;    // log2(e) / sqrt(D)
@@ -214,7 +215,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     const uint64_t q_hi = q_lo + static_cast<uint64_t>(a.BH) * D * 2;
     const uint64_t ks_lo = reinterpret_cast<uint64_t>(a.ks);
     const uint64_t vs_lo = reinterpret_cast<uint64_t>(a.vs);
-    const uint64_t sc_bytes = static_cast<uint64_t>(a.total_rows) * C::kNSub * 2;
+    const uint64_t sc_bytes = static_cast<uint64_t>(a.BH) * a.S_stride * C::kNSub * 2;
     const uint8_t* kbase = static_cast<const uint8_t*>(a.k);
     const uint8_t* vbase = static_cast<const uint8_t*>(a.v);
 
@@ -235,7 +236,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
                 break;
             }
             uint8_t* st = smem + stage * C::kStageBytes;
-            const long long row0 = head0 + t0;
+            const long long row0 = static_cast<long long>(bh) * a.S_stride + t0;  // memory row
             const uint32_t kv_bytes = static_cast<uint32_t>(cnt) * C::kRowBytes;
             uint32_t tx = 2 * kv_bytes;
 
@@ -812,8 +813,9 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                 }
                 int ks_off = 0, vs_off = 0;
                 if constexpr (!kHalfKV) {
-                    ks_off = scale_slot_offset(a.ks, head0 + t0, C::kNSub);
-                    vs_off = scale_slot_offset(a.vs, head0 + t0, C::kNSub);
+                    const long long mrow0 = static_cast<long long>(bh) * a.S_stride + t0;
+                    ks_off = scale_slot_offset(a.ks, mrow0, C::kNSub);
+                    vs_off = scale_slot_offset(a.vs, mrow0, C::kNSub);
                 }
                 consume_tile<D, BS, kHalfKV>(st, sp, cnt, ks_off, vs_off, g, r);
             } else if (t0 == t_a) {

@@ -12,8 +12,8 @@
 // fp16, one 8-byte store of codes); D/8 lanes cover a token row, so a warp
 // handles 32/(D/8) rows per step and the block max is a shuffle reduction
 // over BS/8 lanes.  A grid-stride loop over row groups replaces the
-// reference's one-CTA-per-row launch (16.7 M CTAs at S = 131072), with two
-// row groups in flight per warp.
+// reference's one-CTA-per-row launch (16.7 M CTAs at S = 131072), with
+// kCompressUnroll row groups (their 16-byte loads) in flight per warp.
 #pragma once
 
 #include <cstdint>
@@ -55,6 +55,7 @@ __device__ __forceinline__ float kv_div(float a, float b) {
 }
 
 constexpr int kCompressThreads = 256;
+constexpr int kCompressUnroll = 4;  // row groups whose loads a warp keeps in flight
 
 __device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
     uint4 v;
@@ -80,6 +81,7 @@ template <int D, int BS, int MODE>
 __device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool valid, int c,
                                               uint2* __restrict__ xq,
                                               __half* __restrict__ scales) {
+    // `row` is the destination row of codes and scales
     constexpr int kLPR = D / 8;   // lanes per row
     constexpr int kLPB = BS / 8;  // lanes per block
     constexpr int kNSub = D / BS;
@@ -125,11 +127,20 @@ __device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool val
     }
 }
 
+// Destination row of source row `r` when T rows per head are written at rows
+// [t0, t0 + T) of a cache holding S_cap rows per head (identity when T == S_cap).
+__device__ __forceinline__ long long append_row(long long r, int T, int S_cap, int t0) {
+    if (T == S_cap) return r;
+    const long long bh = r / T;
+    return bh * S_cap + t0 + (r - bh * T);
+}
+
 // x: fp16 rows as uint4 (8 halves each), xq: codes as uint2 (8 bytes each).
+// Source rows are [B*H*T]; see append_row for where they land.
 template <int D, int BS, int MODE>
 __global__ void __launch_bounds__(kCompressThreads)
     kv_compress_kernel(const uint4* __restrict__ x, uint2* __restrict__ xq,
-                       __half* __restrict__ scales, long long rows) {
+                       __half* __restrict__ scales, long long rows, int T, int S_cap, int t0) {
     constexpr int kLPR = D / 8;
     constexpr int kRPW = 32 / kLPR;  // rows per warp step
     const int lane = threadIdx.x & 31;
@@ -138,16 +149,22 @@ __global__ void __launch_bounds__(kCompressThreads)
     const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
-    for (long long r0 = warp * (2 * kRPW); r0 < rows; r0 += nwarps * (2 * kRPW)) {
-        const long long row_a = r0 + rsub;
-        const long long row_b = r0 + kRPW + rsub;
-        const bool va = row_a < rows;
-        const bool vb = row_b < rows;
-        uint4 raw_a = make_uint4(0, 0, 0, 0), raw_b = make_uint4(0, 0, 0, 0);
-        if (va) raw_a = ld_stream_v4(x + row_a * kLPR + c);
-        if (vb) raw_b = ld_stream_v4(x + row_b * kLPR + c);
-        compress_lane<D, BS, MODE>(raw_a, row_a, va, c, xq, scales);
-        compress_lane<D, BS, MODE>(raw_b, row_b, vb, c, xq, scales);
+    constexpr int kU = kCompressUnroll;
+    for (long long r0 = warp * (kU * kRPW); r0 < rows; r0 += nwarps * (kU * kRPW)) {
+        long long row[kU];
+        bool valid[kU];
+        uint4 raw[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            row[u] = r0 + u * kRPW + rsub;
+            valid[u] = row[u] < rows;
+            raw[u] = make_uint4(0, 0, 0, 0);
+            if (valid[u]) raw[u] = ld_stream_v4(x + row[u] * kLPR + c);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            compress_lane<D, BS, MODE>(raw[u], append_row(row[u], T, S_cap, t0), valid[u], c, xq,
+                                       scales);
     }
 }
 

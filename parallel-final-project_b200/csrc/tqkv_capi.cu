@@ -147,14 +147,15 @@ cudaError_t launch_kernel(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t sm
 }
 
 template <int D, int BS>
-tqkv_status compress_impl(const void* x, int8_t* xq, void* scales, long long rows,
-                          cudaStream_t stream) {
+tqkv_status compress_impl(const void* x, int8_t* xq, void* scales, long long rows, int T,
+                          int S_cap, int t0, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return from_cuda(e);
     auto fn = kv_compress_kernel<D, BS, TQKV_COMPRESS_DIV_MODE>;
     const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
-    const long long rows_per_block = 2LL * (kCompressThreads / 32) * (32 / (D / 8));
+    const long long rows_per_block =
+        static_cast<long long>(kCompressUnroll) * (kCompressThreads / 32) * (32 / (D / 8));
     long long grid = (rows + rows_per_block - 1) / rows_per_block;
     const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
     if (grid > cap) grid = cap;
@@ -162,7 +163,7 @@ tqkv_status compress_impl(const void* x, int8_t* xq, void* scales, long long row
     return from_cuda(launch_kernel(fn, dim3(static_cast<unsigned>(grid)), dim3(kCompressThreads), 0,
                                    stream, static_cast<const uint4*>(x),
                                    reinterpret_cast<uint2*>(xq), static_cast<__half*>(scales),
-                                   rows));
+                                   rows, T, S_cap, t0));
 }
 
 template <int D, int BS>
@@ -187,7 +188,7 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
 template <int D, int BS, bool kHalfKV, int OUT>
 tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void* workspace,
                         size_t workspace_bytes, cudaStream_t stream) {
-    // a.peer is set by the caller (kOutPeers) or zero
+    // a.peer is set by the caller (kOutPeers) or zero; a.S_stride by the caller
     using C = DecodeCfg<D, BS, kHalfKV>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -241,6 +242,7 @@ tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void*
     a.vs = static_cast<const uint16_t*>(vs);
     a.out = nullptr;
     a.peer = peer;
+    a.S_stride = S;
     const long long total = static_cast<long long>(BH) * S;
     const OutKind o = OutKind::kPeers;
     if (D == 64 && bs == 32) return decode_out<64, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
@@ -296,12 +298,17 @@ bool is_supported_int8(int D, int block_size) {
 }
 
 tqkv_status launch_compress(const void* x, int8_t* xq, void* scales, long long rows, int D,
-                            int bs, cudaStream_t stream) {
-    if (D == 64 && bs == 32) return compress_impl<64, 32>(x, xq, scales, rows, stream);
-    if (D == 64 && bs == 64) return compress_impl<64, 64>(x, xq, scales, rows, stream);
-    if (D == 128 && bs == 32) return compress_impl<128, 32>(x, xq, scales, rows, stream);
-    if (D == 128 && bs == 64) return compress_impl<128, 64>(x, xq, scales, rows, stream);
-    if (D == 128 && bs == 128) return compress_impl<128, 128>(x, xq, scales, rows, stream);
+                            int bs, cudaStream_t stream, int T, int S_cap, int t0) {
+    if (T <= 0) {  // whole tensors: rows land where they come from
+        T = 1;
+        S_cap = 1;
+        t0 = 0;
+    }
+    if (D == 64 && bs == 32) return compress_impl<64, 32>(x, xq, scales, rows, T, S_cap, t0, stream);
+    if (D == 64 && bs == 64) return compress_impl<64, 64>(x, xq, scales, rows, T, S_cap, t0, stream);
+    if (D == 128 && bs == 32) return compress_impl<128, 32>(x, xq, scales, rows, T, S_cap, t0, stream);
+    if (D == 128 && bs == 64) return compress_impl<128, 64>(x, xq, scales, rows, T, S_cap, t0, stream);
+    if (D == 128 && bs == 128) return compress_impl<128, 128>(x, xq, scales, rows, T, S_cap, t0, stream);
     return TQKV_ERR_UNSUPPORTED;
 }
 
@@ -317,8 +324,10 @@ tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, lo
 
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D, int bs,
-                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                          int S_stride) {
     DecodeArgs a{};
+    a.S_stride = S_stride > 0 ? S_stride : S;
     a.q = q;
     a.k = k;
     a.v = v;
@@ -458,6 +467,35 @@ tqkv_status tqkv_kv_reconstruct(const int8_t* xq, const void* scales, void* y, i
     if (!tqkv::aligned16(xq) || !tqkv::aligned16(y)) return TQKV_ERR_MISALIGNED;
     const long long rows = static_cast<long long>(B) * H * S;
     return tqkv::launch_reconstruct(xq, scales, y, rows, D, block_size, stream);
+}
+
+tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s, int B, int H, int T,
+                           int D, int block_size, int S_cap, int t0, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || T <= 0 || S_cap <= 0 || t0 < 0 ||
+        static_cast<long long>(t0) + T > S_cap)
+        return TQKV_ERR_INVALID_SIZE;
+    if (!x || !cache_q || !cache_s) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(x) || !tqkv::aligned16(cache_q)) return TQKV_ERR_MISALIGNED;
+    const long long rows = static_cast<long long>(B) * H * T;
+    return tqkv::launch_compress(x, cache_q, cache_s, rows, D, block_size, stream, T, S_cap, t0);
+}
+
+tqkv_status tqkv_decode_int8_cache(const void* q, const int8_t* kq, const void* ks,
+                                   const int8_t* vq, const void* vs, void* o, int B, int H, int S,
+                                   int S_cap, int D, int block_size, void* workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || S < 0 || S_cap <= 0 || S > S_cap) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_fill_half(o, BH * D, 0x7e00u, stream);
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode(KvKind::kInt8, OutKind::kHalfO, q, kq, ks, vq, vs, o,
+                               static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
+                               stream, S_cap);
 }
 
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D) {

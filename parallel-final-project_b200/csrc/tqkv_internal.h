@@ -20,14 +20,18 @@ tqkv_status from_cuda(cudaError_t err);
 bool is_supported_int8(int D, int block_size);
 
 // Kernel launches with all checks done by the caller except alignment.
+// T > 0: the rows are T new tokens per head, written to rows [t0, t0 + T) of a
+// cache holding S_cap rows per head; T <= 0: whole tensors, in place.
 tqkv_status launch_compress(const void* x, int8_t* xq, void* scales, long long rows, int D,
-                            int block_size, cudaStream_t stream);
+                            int block_size, cudaStream_t stream, int T = 0, int S_cap = 0,
+                            int t0 = 0);
 tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, long long rows,
                                int D, int block_size, cudaStream_t stream);
+// S rows attended per head; S_stride rows between heads in memory (0: S).
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D,
                           int block_size, void* workspace, size_t workspace_bytes,
-                          cudaStream_t stream);
+                          cudaStream_t stream, int S_stride = 0);
 tqkv_status launch_fill_half(void* o, long long n, uint16_t bits, cudaStream_t stream);
 tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t stream);
 

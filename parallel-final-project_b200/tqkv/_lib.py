@@ -43,6 +43,11 @@ C_ABI = {
     "tqkv_read_device_error": (c_int, [ctypes.POINTER(c_uint32)]),
     "tqkv_decode_int8_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "tqkv_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                               c_int, c_int, c_void_p]),
+    "tqkv_decode_int8_cache": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                       c_size_t, c_void_p]),
     "tqkv_exchange_bytes": (c_size_t, [c_int, c_int, c_int]),
     "tqkv_exchange_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
     "tqkv_exchange_free": (c_int, [c_void_p]),

@@ -67,6 +67,35 @@ def kv_reconstruct(xq: torch.Tensor, scales: torch.Tensor, block_size: int,
     return y
 
 
+def kv_append(x: torch.Tensor, cache_q: torch.Tensor, cache_s: torch.Tensor, t0: int,
+              block_size: int, stream=None) -> None:
+    """Quantise T new tokens per head, x fp16 [B,H,T,D], into rows [t0, t0+T) of
+    the INT8 cache (cache_q int8 [B,H,S_cap,D], cache_s fp16 [B,H,S_cap,D/bs])."""
+    B, H, T, D = _bhsd(x, "x")
+    S_cap = _bhsd(cache_q, "cache_q")[2]
+    lib = load()
+    check("tqkv_kv_append", lib.tqkv_kv_append(
+        _ptr(x), _ptr(cache_q), _ptr(cache_s), B, H, T, D, block_size, S_cap, t0,
+        _stream_handle(stream)))
+
+
+def decode_int8_cache(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor,
+                      vs: torch.Tensor, S: int, block_size: int,
+                      out: Optional[torch.Tensor] = None, workspace: Optional["Workspace"] = None,
+                      stream=None) -> torch.Tensor:
+    """Decode over the first S rows of caches holding S_cap >= S rows per head."""
+    B, H, S_cap, D = _bhsd(kq, "kq")
+    if out is None:
+        out = torch.empty((B, H, D), dtype=_F16, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H, S, D) if S > 0 else 0, stream)
+    lib = load()
+    check("tqkv_decode_int8_cache", lib.tqkv_decode_int8_cache(
+        _ptr(q), _ptr(kq), _ptr(ks), _ptr(vq), _ptr(vs), _ptr(out), B, H, S, S_cap, D,
+        block_size, wptr, wbytes, _stream_handle(stream)))
+    return out
+
+
 def workspace_bytes(B: int, H: int, S: int, D: int) -> int:
     """Scratch the decode kernels need for this shape on the current device."""
     return int(load().tqkv_decode_workspace_bytes(B, H, S, D))

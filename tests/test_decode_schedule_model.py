@@ -51,7 +51,8 @@ def plan_span(src, n, lo, hi):
     return (blo, blo - a16, bhi - blo) if blo < bhi else (0, 0, 0)
 
 
-def check(BH, S, D, bs, half, occ, offs=(0, 0)):
+def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None):
+    S_stride = S if S_stride is None else S_stride
     elem = 2 if half else 1
     RB = D * elem
     LPR = RB // 16
@@ -65,7 +66,8 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0)):
     grid, R, _ = make_plan(total, S, SMS * occ)
     _, _, maxp = make_plan(total, S, SMS * BOUND_OCC)   # workspace layout bound
     kbase, sbase, qbase = 1 << 40, (1 << 41) + offs[0], (1 << 42) + offs[1]
-    s_end, q_end = sbase + total * nsub * 2, qbase + BH * D * 2
+    k_end = kbase + BH * S_stride * RB
+    s_end, q_end = sbase + BH * S_stride * nsub * 2, qbase + BH * D * 2
     covered = 0
     for c in range(grid):
         r0, r1 = c * R, min((c + 1) * R, total)
@@ -81,9 +83,10 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0)):
                 tiles = tiles[:4] + tiles[-4:]
             for t0 in tiles:
                 cnt = min(TILE, tb - t0)
-                row0 = head0 + t0
-                assert 0 < cnt <= TILE and row0 + cnt <= total
+                row0 = bh * S_stride + t0      # memory row, as the kernel computes it
+                assert 0 < cnt <= TILE and t0 + cnt <= S
                 assert (kbase + row0 * RB) % 16 == 0 and cnt * RB % 16 == 0
+                assert kbase <= kbase + row0 * RB and kbase + (row0 + cnt) * RB <= k_end
                 assert cnt * RB <= TILE_BYTES
                 if not half:
                     n = cnt * nsub * 2
@@ -123,6 +126,15 @@ def test_schedule_in_bounds(D, bs, half, occ):
     for BH, S in SHAPES:
         for offs in ((0, 0), (2, 14), (6, 2)):
             check(BH, S, D, bs, half, occ, offs)
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (128, 32), (64, 64)])
+def test_schedule_in_bounds_with_cache_stride(D, bs):
+    """Decode over the first S rows of caches holding S_stride rows per head."""
+    for BH, S, S_stride in [(2, 1, 8), (6, 777, 1000), (6, 4097, 4100), (3, 20000, 32768),
+                            (128, 16384, 16385)]:
+        for offs in ((0, 0), (2, 14)):
+            check(BH, S, D, bs, False, 4, offs, S_stride)
 
 
 def test_stage_layout_fits_four_ctas_per_sm():
