@@ -316,12 +316,31 @@ def main():
             dist.all_gather_into_tensor(gathered, local_rec)
             tqkv.lse_combine(gathered, D, out=out.view(BH, D))
 
+    # End-to-end decode step through the public API: the new token's q, k and
+    # v come from pinned host memory, k and v are appended to the int8 cache
+    # (tqkv_kv_append at the last row of the rank that holds the sequence's
+    # end), the step runs, and O goes back to the host.
     q_host = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     q_host.copy_(q.cpu())
     o_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    owns_last = S_loc > 0 and s1 == w.S
+    kv_new = torch.empty((2, 1, BH_loc, 1, D), dtype=torch.float16, device=dev)
+    kv_new_host = torch.empty(kv_new.shape, dtype=torch.float16, pin_memory=True)
+    if owns_last:
+        # the token being re-appended is the one already cached at the last row
+        # (its fp16 original), so the cache contents stay those of the workload
+        last = W.make_kv_slice(w, "k", w.S - 1, w.S, dev).reshape(1, BH, 1, D)[:, h0:h1]
+        kv_new_host[0].copy_(last.cpu())
+        last = W.make_kv_slice(w, "v", w.S - 1, w.S, dev).reshape(1, BH, 1, D)[:, h0:h1]
+        kv_new_host[1].copy_(last.cpu())
+        del last
 
     def e2e_step():
         q.copy_(q_host, non_blocking=True)
+        if owns_last:
+            kv_new.copy_(kv_new_host, non_blocking=True)
+            tqkv.kv_append(kv_new[0], kq, ks, S_loc - 1, w.block_size)
+            tqkv.kv_append(kv_new[1], vq, vs, S_loc - 1, w.block_size)
         kernel()
         comm()
         o_host.copy_(out, non_blocking=True)
@@ -457,8 +476,11 @@ def main():
         "cpu_baseline": cpu,
         "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "us_per_step": e2e_ms * 1e3,
-                "h2d_bytes_per_step": q.numel() * q.element_size(),
-                "d2h_bytes_per_step": out.numel() * out.element_size()},
+                "h2d_bytes_per_step": q.numel() * q.element_size() +
+                (kv_new.numel() * kv_new.element_size() if owns_last else 0),
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "step": "H2D q, k_new, v_new (pinned) -> append k, v to the int8 cache -> "
+                        "decode -> D2H O -> host sync"},
         "gpu_launches": args.steps * (2 if collective else 1),
         "clocks": clk.summary(),
         "compress": {"us_per_tensor": statistics.mean(comp_us),
