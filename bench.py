@@ -56,6 +56,8 @@ def parse_args():
                    help="multi-GPU split: tokens (s, with NCCL all-gather) or heads (bh, no "
                         "collective); auto = bh for int8_bh_shard, s otherwise")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
+    p.add_argument("--no-kernel-table", action="store_true",
+                   help="skip the per-kernel measurements of compress / reconstruct / fp16 decode")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="split-S record exchange: NVLink peer writes + bounded-wait combine "
                         "(p2p), or NCCL all-gather + combine kernel (nccl, never graph-captured)")
@@ -234,6 +236,52 @@ def run_reference(args, w):
 
 
 # ---------------------------------------------------------------------------
+def kernel_table(w, tqkv, kq, ks, vq, vs, q, comp_us, ws, reps: int = 5):
+    """Each kernel of the path on the workload's own tensors: algorithmic
+    bytes per launch, mean CUDA-event time, GB/s and the fraction of the
+    measured HBM peak.  Kernel C (two-pass INT8) is the same kernel as Kernel D
+    here, so it shares the headline numbers."""
+    peak, _ = measured_peaks()
+    BH, S, D, bs = w.BH, w.S, w.D, w.block_size
+    rows = BH * S
+    scale_b = rows * (D // bs) * 2
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(reps):
+            fn()
+        ev1.record()
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) * 1e3 / reps
+
+    def entry(nbytes, us, what):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        return {"us": us, "algorithmic_bytes": nbytes, "GBps": gbs, "frac_of_peak": gbs / peak,
+                "bytes": what}
+
+    out = {}
+    comp = statistics.mean(comp_us)
+    out["kv_compress (Kernel A), per tensor"] = entry(
+        rows * D * 2 + rows * D + scale_b, comp, "fp16 in + int8 codes + fp16 scales out")
+    k16 = torch.empty(kq.shape, dtype=torch.float16, device=kq.device)
+    v16 = torch.empty_like(k16)
+    us = timed(lambda: tqkv.kv_reconstruct(kq, ks, bs, y=k16))
+    out["kv_reconstruct (Kernel B), per tensor"] = entry(
+        rows * D + scale_b + rows * D * 2, us, "int8 codes + fp16 scales in, fp16 out")
+    tqkv.kv_reconstruct(vq, vs, bs, y=v16)
+    o16 = torch.empty((q.shape[0], q.shape[1], D), dtype=torch.float16, device=q.device)
+    us = timed(lambda: tqkv.decode_fp16(q, k16, v16, out=o16, workspace=ws))
+    out["decode_fp16 (baseline attention)"] = entry(
+        2 * rows * D * 2, us, "fp16 K + V (the reference's fp16 bytes_kv, src/benchmark.cpp:152)")
+    out["decode_int8 two-pass (Kernel C)"] = "same kernel and numbers as Kernel D (headline)"
+    del k16, v16
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse_args()
     from tqkv import workloads as W
@@ -415,6 +463,11 @@ def main():
     e2e_ms_local = ev0.elapsed_time(ev1) / e2e_steps
     del graphs, run_kernel, run_comm, run_e2e
 
+    # ---- the path's other kernels, on this workload (one GPU only) ----
+    kernels = None
+    if world == 1 and not args.no_kernel_table:
+        kernels = kernel_table(w, tqkv, kq, ks, vq, vs, q, comp_us, ws)
+
     # ---- max over ranks ----
     t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, float(err)], device=dev)
     if world > 1:
@@ -487,6 +540,7 @@ def main():
                      "GBps": (w.BH * S_loc * w.D * 3 + w.BH * S_loc * (w.D // w.block_size) * 2)
                      / (statistics.mean(comp_us) * 1e-6) / 1e9},
         "device_error": int(err_max),
+        "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
     return 0

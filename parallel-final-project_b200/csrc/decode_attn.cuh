@@ -57,7 +57,6 @@ constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
 constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeTileBytes = 8192;  // bytes of K (and of V) per stage
 constexpr int kDecodeStages = 3;        // 3 stages x ~17.7 KB: four CTAs fit on an SM
-constexpr int kMergeBarrier = 1;        // named barrier id used by consumers
 
 enum DecodeOut : int {
     kOutHalf = 0,     // write O (fp16)
@@ -109,7 +108,9 @@ struct DecodeArgs {
     float* parts;              // workspace [BH][max_parts][D+2] (log2 units)
     unsigned int* tickets;     // workspace [BH]
     long long total_rows;      // BH * S
-    long long rows_per_cta;    // R
+    long long chunk_rows;      // rows per scheduling chunk (C)
+    unsigned int nchunks;      // ceil(total_rows / C)
+    unsigned int* sched;       // workspace: [0] next chunk to hand out, [1] producers done
     int S;                     // rows attended per head
     int S_stride;              // rows between consecutive heads in K/V/scales (>= S)
     int BH;
@@ -141,13 +142,74 @@ struct DecodeCfg {
     // merge scratch after the ring
     static constexpr int kOffMerge = kDecodeStages * kStageBytes;
     static constexpr int kMergeBytes = kDecodeConsumerWarps * (D + 2) * 4;
+    // the split-head merge reuses it for one weight per consumer thread + 8 sums
+    static_assert(kMergeBytes >= (kDecodeConsumers + 2 * kDecodeConsumerWarps) * 4, "merge area");
     static constexpr int kOffBars = kOffMerge + kMergeBytes;
-    static constexpr int kSmemBytes = kOffBars + 2 * kDecodeStages * 8 + 16;
+    static constexpr int kOffMeta = kOffBars + 2 * kDecodeStages * 8;  // int[stages][8]
+    static constexpr int kOffCtl = kOffMeta + kDecodeStages * 32;      // CtaCtl
+    static constexpr int kSmemBytes = kOffCtl + 32;
 
     static_assert(kTPG == 4, "each lane group owns 4 rows per stage");
     static_assert(kStageBytes % 16 == 0, "stage must stay 16-byte aligned");
     static_assert(kOffMerge % 16 == 0 && kOffBars % 8 == 0, "alignment");
 };
+
+// Per-stage tile descriptor, written by the producer before the stage's
+// mbarrier arrive and read by the consumers after their wait.
+enum TileFlags : int { kTileFirst = 1, kTileLast = 2, kTileDone = 4 };
+struct TileMeta {
+    int bh, t0, cnt, flags, part, nparts, pad0, pad1;
+};
+
+// CTA control block in shared memory: the consumer warps' software barrier
+// (bounded, see consumer_barrier), the merge flag, and an abort flag that any
+// warp whose bounded wait ran out raises so that the others leave as well.
+struct CtaCtl {
+    int flag;
+    unsigned int bar_count;
+    unsigned int bar_gen;
+    unsigned int abort;
+    unsigned int pad[4];
+};
+
+__device__ __forceinline__ unsigned int ld_volatile_shared(const unsigned int* p) {
+    return *reinterpret_cast<const volatile unsigned int*>(p);
+}
+
+// Barrier of the consumer warps.  Unlike bar.sync it cannot hang: a warp that
+// waits longer than ~2^31 cycles, or sees the abort flag, returns false (and
+// raises abort), and the caller leaves the kernel.
+__device__ __forceinline__ bool consumer_barrier(CtaCtl* c) {
+    __threadfence_block();
+    __syncwarp();
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const unsigned int gen = ld_volatile_shared(&c->bar_gen);
+        if (atomicAdd(&c->bar_count, 1u) == static_cast<unsigned int>(kDecodeConsumerWarps - 1)) {
+            c->bar_count = 0u;
+            __threadfence_block();
+            atomicAdd(&c->bar_gen, 1u);
+        } else {
+            const long long start = clock64();
+            while (ld_volatile_shared(&c->bar_gen) == gen) {
+                if (ld_volatile_shared(&c->abort)) {
+                    ok = 0;
+                    break;
+                }
+                if (clock64() - start > (1ll << 31)) {
+                    record_device_error(kErrBarrierTimeout);
+                    atomicExch(&c->abort, 1u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        __threadfence_block();
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
 
 // Bytes [src, src + n) (src even, n even) of the buffer [lo, hi) land in
 // shared memory at dst + (src & 15).  The 16-byte-aligned part that lies
@@ -208,7 +270,7 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) {
 template <int D, int BS, bool kHalfKV>
 __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* smem,
                                                 uint64_t* full, uint64_t* empty,
-                                                long long r0, long long r1) {
+                                                TileMeta* meta, CtaCtl* ctl) {
     using C = DecodeCfg<D, BS, kHalfKV>;
     const uint64_t policy = make_evict_first_policy();
     const uint64_t q_lo = reinterpret_cast<uint64_t>(a.q);
@@ -223,70 +285,124 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     uint32_t phase = 0;
     long long issued = 0;
     bool ok = true;
-    for (long long r = r0; r < r1 && ok;) {
-        const int bh = static_cast<int>(r / a.S);
-        const long long head0 = static_cast<long long>(bh) * a.S;
-        const int t_a = static_cast<int>(r - head0);
-        const int t_b = static_cast<int>((r1 - head0) < a.S ? (r1 - head0) : a.S);
-        for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
-            const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
-            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
-                record_device_error(kErrEmptyWaitTimeout);
-                ok = false;
-                break;
-            }
-            uint8_t* st = smem + stage * C::kStageBytes;
-            const long long row0 = static_cast<long long>(bh) * a.S_stride + t0;  // memory row
-            const uint32_t kv_bytes = static_cast<uint32_t>(cnt) * C::kRowBytes;
-            uint32_t tx = 2 * kv_bytes;
+    // Chunks of C rows are handed out dynamically, so SMs that stream faster
+    // take more of them; chunk boundaries are fixed, which keeps the pieces
+    // of a split head (and their indices) deterministic.
+    unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
+    while (ok) {
+        unsigned int chunk;
+        if (a.sched != nullptr) {
+            chunk = atomicAdd(&a.sched[0], 1u);
+        } else {
+            chunk = static_chunk;
+            static_chunk += gridDim.x;
+        }
+        if (chunk >= a.nchunks) break;
+        const long long c0 = static_cast<long long>(chunk) * a.chunk_rows;
+        const long long c1 = (c0 + a.chunk_rows) < a.total_rows ? c0 + a.chunk_rows : a.total_rows;
+        for (long long r = c0; r < c1 && ok;) {
+            const int bh = static_cast<int>(r / a.S);
+            const long long head0 = static_cast<long long>(bh) * a.S;
+            const int t_a = static_cast<int>(r - head0);
+            const int t_b = static_cast<int>((c1 - head0) < a.S ? (c1 - head0) : a.S);
+            const long long u_first = head0 / a.chunk_rows;
+            const long long u_last = (head0 + a.S - 1) / a.chunk_rows;
+            for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
+                const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
+                if (ld_volatile_shared(&ctl->abort)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+                    record_device_error(kErrEmptyWaitTimeout);
+                    atomicExch(&ctl->abort, 1u);
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + stage * C::kStageBytes;
+                const long long row0 = static_cast<long long>(bh) * a.S_stride + t0;  // memory row
+                const uint32_t kv_bytes = static_cast<uint32_t>(cnt) * C::kRowBytes;
+                uint32_t tx = 2 * kv_bytes;
 
-            Span sk{}, sv{}, sq{};
-            uint64_t ks_src = 0, vs_src = 0, q_src = 0;
-            uint32_t sc_n = 0;
-            if constexpr (!kHalfKV) {
-                sc_n = static_cast<uint32_t>(cnt) * C::kNSub * 2;
-                ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
-                vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
-                sk = plan_span(ks_src, sc_n, ks_lo, ks_lo + sc_bytes);
-                sv = plan_span(vs_src, sc_n, vs_lo, vs_lo + sc_bytes);
-                tx += sk.bulk_bytes + sv.bulk_bytes;
-                copy_span_edges(st + C::kOffKS, ks_src, sc_n, sk);
-                copy_span_edges(st + C::kOffVS, vs_src, sc_n, sv);
-            }
-            const bool first = (t0 == t_a);
-            if (first) {
-                q_src = q_lo + static_cast<uint64_t>(bh) * D * 2;
-                sq = plan_span(q_src, D * 2, q_lo, q_hi);
-                tx += sq.bulk_bytes;
-                copy_span_edges(st + C::kOffQ, q_src, D * 2, sq);
-            }
-            mbar_arrive_expect_tx(&full[stage], tx);
-            bulk_copy_g2s(st + C::kOffK, kbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
-                          policy);
-            bulk_copy_g2s(st + C::kOffV, vbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
-                          policy);
-            if constexpr (!kHalfKV) {
-                if (sk.bulk_bytes)
-                    bulk_copy_g2s(st + C::kOffKS + sk.bulk_dst_off,
-                                  reinterpret_cast<const void*>(sk.bulk_src), sk.bulk_bytes,
+                TileMeta& m = meta[stage];
+                m.bh = bh;
+                m.t0 = t0;
+                m.cnt = cnt;
+                m.flags = (t0 == t_a ? kTileFirst : 0) | (t0 + C::kTile >= t_b ? kTileLast : 0);
+                m.part = static_cast<int>(chunk - u_first);
+                m.nparts = static_cast<int>(u_last - u_first + 1);
+
+                Span sk{}, sv{}, sq{};
+                uint64_t ks_src = 0, vs_src = 0, q_src = 0;
+                uint32_t sc_n = 0;
+                if constexpr (!kHalfKV) {
+                    sc_n = static_cast<uint32_t>(cnt) * C::kNSub * 2;
+                    ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                    vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                    sk = plan_span(ks_src, sc_n, ks_lo, ks_lo + sc_bytes);
+                    sv = plan_span(vs_src, sc_n, vs_lo, vs_lo + sc_bytes);
+                    tx += sk.bulk_bytes + sv.bulk_bytes;
+                    copy_span_edges(st + C::kOffKS, ks_src, sc_n, sk);
+                    copy_span_edges(st + C::kOffVS, vs_src, sc_n, sv);
+                }
+                const bool first = (t0 == t_a);
+                if (first) {
+                    q_src = q_lo + static_cast<uint64_t>(bh) * D * 2;
+                    sq = plan_span(q_src, D * 2, q_lo, q_hi);
+                    tx += sq.bulk_bytes;
+                    copy_span_edges(st + C::kOffQ, q_src, D * 2, sq);
+                }
+                mbar_arrive_expect_tx(&full[stage], tx);
+                bulk_copy_g2s(st + C::kOffK, kbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
+                              policy);
+                bulk_copy_g2s(st + C::kOffV, vbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
+                              policy);
+                if constexpr (!kHalfKV) {
+                    if (sk.bulk_bytes)
+                        bulk_copy_g2s(st + C::kOffKS + sk.bulk_dst_off,
+                                      reinterpret_cast<const void*>(sk.bulk_src), sk.bulk_bytes,
+                                      &full[stage], policy);
+                    if (sv.bulk_bytes)
+                        bulk_copy_g2s(st + C::kOffVS + sv.bulk_dst_off,
+                                      reinterpret_cast<const void*>(sv.bulk_src), sv.bulk_bytes,
+                                      &full[stage], policy);
+                }
+                if (first && sq.bulk_bytes) {
+                    bulk_copy_g2s(st + C::kOffQ + sq.bulk_dst_off,
+                                  reinterpret_cast<const void*>(sq.bulk_src), sq.bulk_bytes,
                                   &full[stage], policy);
-                if (sv.bulk_bytes)
-                    bulk_copy_g2s(st + C::kOffVS + sv.bulk_dst_off,
-                                  reinterpret_cast<const void*>(sv.bulk_src), sv.bulk_bytes,
-                                  &full[stage], policy);
+                }
+                ++issued;
+                if (++stage == kDecodeStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
             }
-            if (first && sq.bulk_bytes) {
-                bulk_copy_g2s(st + C::kOffQ + sq.bulk_dst_off,
-                              reinterpret_cast<const void*>(sq.bulk_src), sq.bulk_bytes,
-                              &full[stage], policy);
-            }
+            r = head0 + t_b;
+        }
+    }
+    // end-of-work marker for the consumers
+    if (ok) {
+        if (mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+            meta[stage].flags = kTileDone;
+            mbar_arrive(&full[stage]);
             ++issued;
             if (++stage == kDecodeStages) {
                 stage = 0;
                 phase ^= 1u;
             }
+        } else {
+            record_device_error(kErrEmptyWaitTimeout);
+            atomicExch(&ctl->abort, 1u);
         }
-        r = head0 + t_b;
+    }
+    // the last producer to finish hands the scheduler back zeroed: every
+    // producer has taken its final (empty) chunk before counting itself out
+    __threadfence();
+    if (a.sched != nullptr && atomicAdd(&a.sched[1], 1u) == gridDim.x - 1) {
+        __threadfence();
+        atomicExch(&a.sched[0], 0u);
+        atomicExch(&a.sched[1], 0u);
     }
     // Drain: do not leave the CTA while copies into its shared memory are in
     // flight.  In a normal run every stage was consumed long ago.
@@ -634,13 +750,13 @@ __device__ __forceinline__ void emit_head(const DecodeArgs& a, int bh, int tid, 
 }
 
 // Finish one segment: merge the lane-group states of the CTA, then either
-// write O / the partial record (head owned by this CTA alone), or publish a
-// partial and let the last CTA of the head merge all of them.
+// write O / the partial record (head held by one chunk), or publish a partial
+// and let the last chunk of the head to finish merge all of them.  Returns
+// false when a consumer barrier gave up (the CTA then leaves).
 template <int D, int BS, bool kHalfKV, int OUT>
-__device__ __forceinline__ unsigned int finish_segment(SegState<D, BS, kHalfKV>& st,
-                                                       const DecodeArgs& a, float* merge,
-                                                       int* flag, int bh, int part, int nparts,
-                                                       int tid) {
+__device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, const DecodeArgs& a,
+                                               float* merge, CtaCtl* ctl, int bh, int part,
+                                               int nparts, int tid) {
     using C = DecodeCfg<D, BS, kHalfKV>;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -684,7 +800,7 @@ __device__ __forceinline__ unsigned int finish_segment(SegState<D, BS, kHalfKV>&
             mw[D + 1] = st.l;
         }
     }
-    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+    if (!consumer_barrier(ctl)) return false;
 
     float A = 0.0f, M = -INFINITY, L = 0.0f;
     if (tid < D) {
@@ -701,8 +817,7 @@ __device__ __forceinline__ unsigned int finish_segment(SegState<D, BS, kHalfKV>&
 
     if (nparts == 1) {
         emit_head<D, OUT>(a, bh, tid, A, M, L);
-        named_barrier_sync(kMergeBarrier, kDecodeConsumers);  // merge[] reused next segment
-        return 1u;
+        return consumer_barrier(ctl);  // merge[] is reused by the next segment
     }
 
     // publish this CTA's piece of the head
@@ -715,35 +830,65 @@ __device__ __forceinline__ unsigned int finish_segment(SegState<D, BS, kHalfKV>&
         }
     }
     __threadfence();
-    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
+    if (!consumer_barrier(ctl)) return false;
     if (tid == 0) {
         const unsigned int prev = atomicAdd(&a.tickets[bh], 1u);
-        *flag = (prev == static_cast<unsigned int>(nparts - 1)) ? 1 : 0;
+        ctl->flag = (prev == static_cast<unsigned int>(nparts - 1)) ? 1 : 0;
     }
-    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
-    if (*flag) {
+    if (!consumer_barrier(ctl)) return false;
+    if (*reinterpret_cast<volatile int*>(&ctl->flag)) {
+        // Last piece of the head: merge its nparts records.  The records are
+        // spread over the consumer threads (one per thread for the maxima and
+        // weights) so the L2 reads overlap instead of running one by one.
         __threadfence();
         const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
-        float Mt = -INFINITY, At = 0.0f, Lt = 0.0f;
-        if (tid < D) {
-            for (int p = 0; p < nparts; ++p) Mt = fmaxf(Mt, __ldcg(recs + p * (D + 2) + D));
-            const float base = Mt == -INFINITY ? 0.0f : Mt;
-            for (int p = 0; p < nparts; ++p) {
-                const float f = fast_exp2(__ldcg(recs + p * (D + 2) + D) - base);
-                Lt = fmaf(__ldcg(recs + p * (D + 2) + D + 1), f, Lt);
-                At = fmaf(__ldcg(recs + p * (D + 2) + tid), f, At);
+        float* fw = merge;                          // weights of one batch of records
+        float* red = merge + kDecodeConsumers;      // [0..3] warp maxima, [4..7] warp sums
+        float mloc = -INFINITY;
+        for (int p = tid; p < nparts; p += kDecodeConsumers)
+            mloc = fmaxf(mloc, __ldcg(recs + p * (D + 2) + D));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
+        if (lane == 0) red[warp] = mloc;
+        if (!consumer_barrier(ctl)) return false;
+        float Mt = red[0];
+#pragma unroll
+        for (int w = 1; w < kDecodeConsumerWarps; ++w) Mt = fmaxf(Mt, red[w]);
+        const float base = Mt == -INFINITY ? 0.0f : Mt;
+        float At = 0.0f, Lloc = 0.0f;
+        for (int b0 = 0; b0 < nparts; b0 += kDecodeConsumers) {
+            const int nb = (nparts - b0) < kDecodeConsumers ? (nparts - b0) : kDecodeConsumers;
+            if (tid < nb) {
+                const float* rp = recs + (b0 + tid) * (D + 2);
+                const float f = fast_exp2(__ldcg(rp + D) - base);
+                fw[tid] = f;
+                Lloc = fmaf(__ldcg(rp + D + 1), f, Lloc);
             }
+            if (!consumer_barrier(ctl)) return false;
+            if (tid < D) {
+                const float* rp = recs + b0 * (D + 2) + tid;
+#pragma unroll 8
+                for (int k = 0; k < nb; ++k) At = fmaf(__ldcg(rp + k * (D + 2)), fw[k], At);
+            }
+            if (b0 + kDecodeConsumers < nparts && !consumer_barrier(ctl)) return false;
         }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Lloc += __shfl_xor_sync(0xffffffffu, Lloc, off);
+        if (lane == 0) red[kDecodeConsumerWarps + warp] = Lloc;
+        // every record has been read once all warps pass this barrier
+        if (!consumer_barrier(ctl)) return false;
+        float Lt = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDecodeConsumerWarps; ++w) Lt += red[kDecodeConsumerWarps + w];
         emit_head<D, OUT>(a, bh, tid, At, Mt, Lt);
         // leave the workspace all-zero for the next call, whatever its shape:
         // the ticket, and every record this merge consumed
-        named_barrier_sync(kMergeBarrier, kDecodeConsumers);
         float* zrec = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
         for (int i = tid; i < nparts * (D + 2); i += kDecodeConsumers) zrec[i] = 0.0f;
         if (tid == 0) a.tickets[bh] = 0u;
     }
-    named_barrier_sync(kMergeBarrier, kDecodeConsumers);
-    return *flag ? 1u : 0u;
+    return consumer_barrier(ctl);
 }
 
 // ---------------------------------------------------------------------------
@@ -756,26 +901,26 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
     uint64_t* empty = full + kDecodeStages;
-    int* flag = reinterpret_cast<int*>(empty + kDecodeStages);
+    TileMeta* meta = reinterpret_cast<TileMeta*>(smem + C::kOffMeta);
+    CtaCtl* ctl = reinterpret_cast<CtaCtl*>(smem + C::kOffCtl);
     float* merge = reinterpret_cast<float*>(smem + C::kOffMerge);
-
-    const long long r0 = static_cast<long long>(blockIdx.x) * a.rows_per_cta;
-    const long long r1_raw = r0 + a.rows_per_cta;
-    const long long r1 = r1_raw < a.total_rows ? r1_raw : a.total_rows;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecodeStages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kDecodeConsumerWarps);
         }
+        ctl->flag = 0;
+        ctl->bar_count = 0u;
+        ctl->bar_gen = 0u;
+        ctl->abort = 0u;
         fence_barrier_init();
     }
     __syncthreads();
-    if (r0 >= r1) return;
 
     const int warp = threadIdx.x >> 5;
     if (warp == kDecodeConsumerWarps) {
-        if ((threadIdx.x & 31) == 0) decode_producer<D, BS, kHalfKV>(a, smem, full, empty, r0, r1);
+        if ((threadIdx.x & 31) == 0) decode_producer<D, BS, kHalfKV>(a, smem, full, empty, meta, ctl);
         return;
     }
 
@@ -786,61 +931,43 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     int stage = 0;
     uint32_t phase = 0;
     SegState<D, BS, kHalfKV> st;
-    // A warp whose bounded wait ran out stops computing but keeps walking the
-    // schedule, so that the consumer-wide named barriers still see every warp.
-    bool broken = false;
-    unsigned int emitted = 0;  // heads this CTA finished (kOutPeers bookkeeping)
 
-    for (long long rr = r0; rr < r1;) {
-        const int bh = static_cast<int>(rr / a.S);
-        const long long head0 = static_cast<long long>(bh) * a.S;
-        const int t_a = static_cast<int>(rr - head0);
-        const int t_b = static_cast<int>((r1 - head0) < a.S ? (r1 - head0) : a.S);
-        for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
-            const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
-            if (!broken) {
-                const bool ok = mbar_wait_bounded(&full[stage], phase);
-                broken = __any_sync(0xffffffffu, !ok);
-                if (broken && lane == 0) record_device_error(kErrFullWaitTimeout);
+    for (;;) {
+        const bool ok = mbar_wait_bounded(&full[stage], phase);
+        // warp-uniform decision: every lane leaves, or none does
+        if (__any_sync(0xffffffffu, !ok || ld_volatile_shared(&ctl->abort) != 0u)) {
+            if (lane == 0) {
+                if (!ok) record_device_error(kErrFullWaitTimeout);
+                atomicExch(&ctl->abort, 1u);
             }
-            const uint8_t* sp = smem + stage * C::kStageBytes;
-            if (!broken) {
-                if (t0 == t_a) {
-                    const int q_off = static_cast<int>(
-                        (reinterpret_cast<uint64_t>(a.q) + static_cast<uint64_t>(bh) * D * 2) &
-                        15);
-                    load_q<D, BS, kHalfKV>(st, sp + C::kOffQ + q_off, r, a.score_scale_log2);
-                }
-                int ks_off = 0, vs_off = 0;
-                if constexpr (!kHalfKV) {
-                    const long long mrow0 = static_cast<long long>(bh) * a.S_stride + t0;
-                    ks_off = scale_slot_offset(a.ks, mrow0, C::kNSub);
-                    vs_off = scale_slot_offset(a.vs, mrow0, C::kNSub);
-                }
-                consume_tile<D, BS, kHalfKV>(st, sp, cnt, ks_off, vs_off, g, r);
-            } else if (t0 == t_a) {
-                st.m2 = -INFINITY;
-                st.mx = -INFINITY;
-                st.l = 0.0f;
-#pragma unroll
-                for (int i = 0; i < C::kEPL / 2; ++i) st.acc[i] = make_float2(0.0f, 0.0f);
-            }
-            __syncwarp();
-            if (lane == 0 && !broken) mbar_arrive(&empty[stage]);
-            if (++stage == kDecodeStages) {
-                stage = 0;
-                phase ^= 1u;
-            }
+            return;
         }
-        // which CTAs hold pieces of this head
-        const long long c_first = head0 / a.rows_per_cta;
-        const long long c_last = (head0 + a.S - 1) / a.rows_per_cta;
-        const int nparts = static_cast<int>(c_last - c_first + 1);
-        const int part = static_cast<int>(blockIdx.x - c_first);
-        emitted += finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, flag, bh, part, nparts, tid);
-        rr = head0 + t_b;
+        const TileMeta m = meta[stage];
+        if (m.flags & kTileDone) return;
+        const uint8_t* sp = smem + stage * C::kStageBytes;
+        if (m.flags & kTileFirst) {
+            const int q_off = static_cast<int>(
+                (reinterpret_cast<uint64_t>(a.q) + static_cast<uint64_t>(m.bh) * D * 2) & 15);
+            load_q<D, BS, kHalfKV>(st, sp + C::kOffQ + q_off, r, a.score_scale_log2);
+        }
+        int ks_off = 0, vs_off = 0;
+        if constexpr (!kHalfKV) {
+            const long long mrow0 = static_cast<long long>(m.bh) * a.S_stride + m.t0;
+            ks_off = scale_slot_offset(a.ks, mrow0, C::kNSub);
+            vs_off = scale_slot_offset(a.vs, mrow0, C::kNSub);
+        }
+        consume_tile<D, BS, kHalfKV>(st, sp, m.cnt, ks_off, vs_off, g, r);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == kDecodeStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+        if (m.flags & kTileLast) {
+            if (!finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, ctl, m.bh, m.part, m.nparts, tid))
+                return;
+        }
     }
-    (void)emitted;
 }
 
 // Log-sum-exp merge of R partial records per head (natural-log units):

@@ -20,7 +20,8 @@ enum DeviceErrorCode : unsigned int {
     kErrFullWaitTimeout = 1,     // consumer waited too long for a tile
     kErrEmptyWaitTimeout = 2,    // producer waited too long for a free stage
     kErrDrainTimeout = 3,        // producer's copies never completed
-    kErrPeerWaitTimeout = 4,     // a peer GPU's exchange flag never arrived
+    kErrPeerWaitTimeout = 4,     // a peer GPU's exchange entries never arrived
+    kErrBarrierTimeout = 5,      // a consumer warp never reached a CTA barrier
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {

@@ -40,6 +40,8 @@ namespace {
 thread_local int t_last_cuda_error = 0;
 
 constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipeline fill
+constexpr long long kChunksPerCta = 8;     // scheduling chunks per CTA (load balance)
+constexpr long long kChunkAlign = 128;     // chunk rows: a multiple of every tile height
 constexpr int kMaxCtasPerSmBound = 4;      // >= any decode kernel's occupancy (smem-bound)
 
 struct KernelKey {
@@ -87,21 +89,30 @@ int prepare_kernel(Fn fn, int threads, int smem_bytes, int device) {
 
 struct DecodePlan {
     int grid;
-    long long rows_per_cta;
+    long long chunk_rows;
+    long long nchunks;
     int max_parts;
 };
 
-// Equal runs of rows per CTA.  `max_ctas` caps the grid (resident CTAs).
+// Rows are cut into fixed chunks of C rows that the CTAs claim dynamically,
+// about kChunksPerCta per CTA, so SMs that stream faster take more chunks.
+// `max_ctas` caps the grid (resident CTAs).  One CTA takes everything as one
+// chunk.  C does not grow with max_ctas, so a bound plan computed with the
+// largest grid has the most parts per head.
 DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
     DecodePlan p{};
     long long g = (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta;
     if (g > max_ctas) g = max_ctas;
     if (g < 1) g = 1;
-    long long r = (total_rows + g - 1) / g;
-    r = (r + 15) / 16 * 16;  // keeps 16-token alignment of run starts when S allows it
-    p.rows_per_cta = r;
-    p.grid = static_cast<int>((total_rows + r - 1) / r);
-    p.max_parts = static_cast<int>((static_cast<long long>(S) - 1) / r + 2);
+    long long c = total_rows;
+    if (g > 1) {
+        c = (total_rows + g * kChunksPerCta - 1) / (g * kChunksPerCta);
+        c = (c + kChunkAlign - 1) / kChunkAlign * kChunkAlign;
+    }
+    p.chunk_rows = c;
+    p.nchunks = (total_rows + c - 1) / c;
+    p.grid = static_cast<int>(p.nchunks < g ? p.nchunks : g);
+    p.max_parts = static_cast<int>((static_cast<long long>(S) - 1) / c + 2);
     return p;
 }
 
@@ -114,14 +125,17 @@ DecodePlan bound_plan(long long total_rows, int S, int device) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// [0, 16): chunk scheduler counters; [16, ...): one ticket per head; then,
+// 256-aligned, max_parts partial records per head.  All zero between calls.
 struct WsLayout {
-    size_t tickets_off, parts_off, total;
+    size_t sched_off, tickets_off, parts_off, total;
 };
 
 WsLayout ws_layout(long long BH, int max_parts, int D) {
     WsLayout w{};
-    w.tickets_off = 0;
-    w.parts_off = align_up(static_cast<size_t>(BH) * sizeof(unsigned int), 256);
+    w.sched_off = 0;
+    w.tickets_off = 16;
+    w.parts_off = decode_ws_counter_bytes(BH);
     w.total = w.parts_off +
               align_up(static_cast<size_t>(BH) * max_parts * (D + 2) * sizeof(float), 256);
     return w;
@@ -202,14 +216,16 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     const long long resident = static_cast<long long>(sm_count(dev)) * per_sm;
     const DecodePlan plan = make_plan(total_rows, S, resident);
     if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: per_sm <= bound
-    const bool needs_ws = plan.grid > 1;
+    const bool needs_ws = plan.nchunks > 1;
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.sched = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.sched_off) : nullptr;
     a.tickets = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.tickets_off) : nullptr;
     a.parts = needs_ws ? reinterpret_cast<float*>(ws + lay.parts_off) : nullptr;
     a.total_rows = total_rows;
-    a.rows_per_cta = plan.rows_per_cta;
+    a.chunk_rows = plan.chunk_rows;
+    a.nchunks = static_cast<unsigned int>(plan.nchunks);
     a.S = S;
     a.BH = BH;
     a.max_parts = bound.max_parts;
@@ -363,6 +379,10 @@ tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t
     if (grid > 1024) grid = 1024;
     return from_cuda(launch_kernel(fill_empty_partials_kernel, dim3(static_cast<unsigned>(grid)),
                                    dim3(256), 0, stream, p, heads, D));
+}
+
+size_t decode_ws_counter_bytes(long long BH) {
+    return align_up(16 + static_cast<size_t>(BH) * sizeof(unsigned int), 256);
 }
 
 size_t decode_workspace_bytes(long long BH, int S, int D) {
@@ -733,13 +753,13 @@ extern "C" tqkv_status tqkv_decode_int8_noalloc(const void* q, const int8_t* kq,
     void* scratch = nullptr;
     tqkv_status st = tqkv::noalloc_scratch_address(&scratch);
     if (st != TQKV_OK) return st;
-    // The array keeps whatever the previous call left.  Only the ticket
-    // counters at its start must be zero when a launch begins (partial records
-    // are always written before they are read); a completed call leaves them
-    // zero, an interrupted one might not, so clear them every time.
-    const size_t ticket_bytes = (static_cast<size_t>(BH) * sizeof(unsigned int) + 255) / 256 * 256;
+    // The array keeps whatever the previous call left.  Only the scheduler and
+    // ticket counters at its start must be zero when a launch begins (partial
+    // records are always written before they are read); a completed call
+    // leaves them zero, an interrupted one might not, so clear them every time.
+    const size_t counter_bytes = tqkv::decode_ws_counter_bytes(BH);
     if (need > 0) {
-        st = tqkv::from_cuda(cudaMemsetAsync(scratch, 0, ticket_bytes, stream));
+        st = tqkv::from_cuda(cudaMemsetAsync(scratch, 0, counter_bytes, stream));
         if (st != TQKV_OK) return st;
     }
     return tqkv::launch_decode(tqkv::KvKind::kInt8, tqkv::OutKind::kHalfO, q, kq, ks, vq, vs, o,

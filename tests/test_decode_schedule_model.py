@@ -2,10 +2,12 @@
 
 Compute-sanitizer is not available for this kernel's GPU runs, so its bounds
 are established here instead: the host plan (make_plan in tqkv_capi.cu), the
-producer's tile loop and bulk-copy spans, the consumers' shared-memory reads
-and the workspace part indices (decode_attn.cuh) are re-enacted for many
-shapes, asserting that
-  * every token row of every head is covered exactly once;
+producer's chunk and tile loops and bulk-copy spans, the consumers' shared-
+memory reads and the workspace part indices (decode_attn.cuh) are re-enacted
+for many shapes, asserting that
+  * every token row of every head is covered exactly once, whichever CTA
+    claims which chunk (chunks are handed out dynamically, so the model walks
+    chunks rather than CTAs);
   * every bulk copy is 16-byte aligned, a multiple of 16 bytes, inside its
     global buffer and inside its shared-memory slot;
   * every plain edge load is inside its buffer and its slot;
@@ -33,15 +35,21 @@ TILE_BYTES = _const("decode_attn.cuh", "kDecodeTileBytes")
 STAGES = _const("decode_attn.cuh", "kDecodeStages")
 WARPS = _const("decode_attn.cuh", "kDecodeConsumerWarps")
 MIN_ROWS = _const("tqkv_capi.cu", "kMinRowsPerCta")
+CHUNKS_PER_CTA = _const("tqkv_capi.cu", "kChunksPerCta")
+CHUNK_ALIGN = _const("tqkv_capi.cu", "kChunkAlign")
 BOUND_OCC = _const("tqkv_capi.cu", "kMaxCtasPerSmBound")
 SMS = 148
 
 
 def make_plan(total, S, max_ctas):
+    """(grid, chunk rows C, number of chunks, max_parts)"""
     g = max(min(-(-total // MIN_ROWS), max_ctas), 1)
-    r = -(-total // g)
-    r = -(-r // 16) * 16
-    return -(-total // r), r, (S - 1) // r + 2
+    c = total
+    if g > 1:
+        c = -(-total // (g * CHUNKS_PER_CTA))
+        c = -(-c // CHUNK_ALIGN) * CHUNK_ALIGN
+    n = -(-total // c)
+    return min(n, g), c, n, (S - 1) // c + 2
 
 
 def plan_span(src, n, lo, hi):
@@ -63,13 +71,16 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None):
     slot = 0 if half else TILE * nsub * 2 + 32
     qslot = D * 2 + 32
     total = BH * S
-    grid, R, _ = make_plan(total, S, SMS * occ)
-    _, _, maxp = make_plan(total, S, SMS * BOUND_OCC)   # workspace layout bound
+    grid, R, nchunks, _ = make_plan(total, S, SMS * occ)
+    _, _, _, maxp = make_plan(total, S, SMS * BOUND_OCC)   # workspace layout bound
+    assert 1 <= grid <= nchunks and nchunks < 2 ** 32
+    if nchunks == 1:      # no workspace: every head must be one piece
+        assert R >= total
     kbase, sbase, qbase = 1 << 40, (1 << 41) + offs[0], (1 << 42) + offs[1]
     k_end = kbase + BH * S_stride * RB
     s_end, q_end = sbase + BH * S_stride * nsub * 2, qbase + BH * D * 2
     covered = 0
-    for c in range(grid):
+    for c in range(nchunks):
         r0, r1 = c * R, min((c + 1) * R, total)
         assert r0 < r1
         r = r0
@@ -138,10 +149,11 @@ def test_schedule_in_bounds_with_cache_stride(D, bs):
 
 
 def test_stage_layout_fits_four_ctas_per_sm():
-    """3-stage ring + merge scratch + barriers of the largest instantiation
-    (INT8, D = 128, bs = 32) leave room for four CTAs in 228 KB."""
+    """3-stage ring + merge scratch + barriers + tile descriptors + control
+    block of the largest instantiation (INT8, D = 128, bs = 32) leave room for
+    four CTAs in 228 KB."""
     RB, nsub = 128, 4
     TILE = TILE_BYTES // RB
     stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (128 * 2 + 32)
-    smem = STAGES * stage + WARPS * (128 + 2) * 4 + 2 * STAGES * 8 + 16
+    smem = STAGES * stage + WARPS * (128 + 2) * 4 + 2 * STAGES * 8 + STAGES * 32 + 32
     assert 4 * (smem + 1024) <= 228 * 1024, smem
