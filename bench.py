@@ -7,13 +7,21 @@
 One step = one decode step of the whole workload: every head's attention of
 one query over its int8 KV cache (K and V codes plus fp16 block scales,
 resident in HBM).  Default workload: B4 H32 D128 S131072, block size 128
-(4.36 GB of KV per step, far above the 126 MB L2, so no L2 flush is needed).
+(4.36 GB of KV per step, far above the 126 MB L2, so no L2 flush is needed;
+a rank whose KV is under twice the L2 gets the L2 overwritten between timed
+steps, and the L2-hot figure is reported beside it).
 
 Multi-GPU (torchrun, one process per GPU): the S tokens of every head are
-split across ranks; each rank runs the split-S partial kernel on its slice,
-the per-head (acc, m, l) records are all-gathered over NCCL, and every rank
+split across ranks; each rank runs the decode kernel on its slice, the
+per-head (acc, m, l) records are exchanged through NVLink peer mappings
+(default; or all-gathered over NCCL with --exchange nccl), and every rank
 merges them with the log-sum-exp combine kernel.  Total work is fixed, so
-scaling is strong.  Time is device time (CUDA events), max over ranks.
+scaling is strong.  --shard bh splits heads instead, with no collective.
+Time is device time (CUDA events), max over ranks.
+
+The end-to-end figure (e2e) runs each step through the public API from pinned
+host memory: H2D of q and the new token's k, v; decode with the append of
+k, v fused into the same launch; D2H of O.
 
 Rank 0 prints one JSON line.  --impl reference times the reference's CPU
 formulation of the same step (its Python check's dequantise + fp32
@@ -387,9 +395,17 @@ def main():
         q.copy_(q_host, non_blocking=True)
         if owns_last:
             kv_new.copy_(kv_new_host, non_blocking=True)
-            tqkv.kv_append(kv_new[0], kq, ks, S_loc - 1, w.block_size)
-            tqkv.kv_append(kv_new[1], vq, vs, S_loc - 1, w.block_size)
-        kernel()
+        if owns_last and not collective:      # append fused into the decode launch
+            tqkv.decode_int8_append(q, kv_new[0], kv_new[1], kq, ks, vq, vs, S_loc,
+                                    w.block_size, out=out, workspace=ws)
+        elif owns_last and use_p2p:
+            exchange.publish_append(q, kv_new[0], kv_new[1], kq, ks, vq, vs, S_loc,
+                                    w.block_size, workspace=ws)
+        else:
+            if owns_last:                     # NCCL path: separate append launches
+                tqkv.kv_append(kv_new[0], kq, ks, S_loc - 1, w.block_size)
+                tqkv.kv_append(kv_new[1], vq, vs, S_loc - 1, w.block_size)
+            kernel()
         comm()
         o_host.copy_(out, non_blocking=True)
 
@@ -411,12 +427,17 @@ def main():
                 fn()
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
-        for fn in (kernel, comm, e2e_step):
+        captured = []
+        for fn in ((kernel, comm, e2e_step) if collective else (kernel, e2e_step)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
             graphs.append(g)
-        run_kernel, run_comm, run_e2e = (g.replay for g in graphs)
+            captured.append(g.replay)
+        if collective:
+            run_kernel, run_comm, run_e2e = captured
+        else:                   # one GPU: nothing to exchange
+            (run_kernel, run_e2e), run_comm = captured, comm
     else:
         run_kernel, run_comm, run_e2e = kernel, comm, e2e_step
     graphs_used = len(graphs) > 0
@@ -425,8 +446,16 @@ def main():
         run_comm()
     torch.cuda.synchronize()
 
+    # A rank whose KV is smaller than twice the L2 gets the L2 overwritten
+    # between timed steps (outside the timed events), so every step reads its
+    # KV from HBM; back-to-back (L2-hot) steps are reported beside it.
+    local_bytes = w.kv_bytes_int8(S_loc) * BH_loc // BH
+    l2_bytes = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush_buf = (torch.empty(2 * l2_bytes, dtype=torch.uint8, device=dev)
+                 if local_bytes < 2 * l2_bytes else None)
+
     # ---- timed region: exactly K steps ----
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
            for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
@@ -434,16 +463,34 @@ def main():
         torch.cuda.nvtx.range_push("tqkv_timed")  # lets ncu --nvtx-include select this region
         ev0.record()
         for i in range(args.steps):
+            if flush_buf is not None:
+                flush_buf.zero_()
             kev[i][0].record()
             run_kernel()
             kev[i][1].record()
             run_comm()
+            kev[i][2].record()
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     barrier()
-    step_ms_local = ev0.elapsed_time(ev1) / args.steps
-    kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    if flush_buf is None:
+        step_ms_local = ev0.elapsed_time(ev1) / args.steps
+    else:
+        step_ms_local = statistics.mean(a.elapsed_time(c) for a, _, c in kev)
+    kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    hot_ms_local = step_ms_local
+    if flush_buf is not None:     # the same steps back to back, KV left in L2
+        torch.cuda.synchronize()
+        barrier()
+        ev0.record()
+        for i in range(args.steps):
+            run_kernel()
+            run_comm()
+        ev1.record()
+        torch.cuda.synchronize()
+        barrier()
+        hot_ms_local = ev0.elapsed_time(ev1) / args.steps
     err = tqkv.read_device_error()
 
     # ---- end to end through the public API: H2D q, decode, D2H O, per step ----
@@ -469,13 +516,13 @@ def main():
         kernels = kernel_table(w, tqkv, kq, ks, vq, vs, q, comp_us, ws)
 
     # ---- max over ranks ----
-    t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, float(err)], device=dev)
+    t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, hot_ms_local, float(err)],
+                     device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, kern_ms, e2e_ms, err_max = t.tolist()
+    step_ms, kern_ms, e2e_ms, hot_ms, err_max = t.tolist()
 
     total_bytes = w.kv_bytes_int8()
-    local_bytes = w.kv_bytes_int8(S_loc) * BH_loc // BH
     peak, peak_kind = measured_peaks()
     value = total_bytes / (step_ms * 1e-3) / 1e9
     achieved = local_bytes / (kern_ms * 1e-3) / 1e9
@@ -510,7 +557,7 @@ def main():
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8 codes, s32 dp4a K-dot, fp32 softmax/V",
-        "data": "synthetic (seeded N(0,1) K/V/q, generated on device)",
+        "data": f"synthetic, generated on device: {w.description}",
         "config": {
             "workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D,
             "block_size": w.block_size, "global_batch": w.B, "seq_len": w.S,
@@ -518,7 +565,11 @@ def main():
                             f"split-S x{world} + NCCL all-gather" if collective else
                             f"B*H shards x{world}, no collective" if world > 1 else "1 GPU"),
             "cuda_graphs": bool(graphs_used),
-            "l2": f"inputs {total_bytes / 1e9:.2f} GB per step > 126 MB L2; no flush needed",
+            "l2": (f"KV {local_bytes / 1e6:.1f} MB per GPU per step >= 2x the "
+                   f"{l2_bytes / 1e6:.0f} MB L2; no flush needed" if flush_buf is None else
+                   f"KV {local_bytes / 1e6:.1f} MB per GPU per step < 2x the {l2_bytes / 1e6:.0f} "
+                   f"MB L2: L2 overwritten ({2 * l2_bytes / 1e6:.0f} MB memset) before every "
+                   f"timed step, outside the step's events"),
         },
         "roofline": {
             "bound": "hbm", "kernel": DECODE_KERNEL + (" (split-S partial)" if collective else ""),
@@ -532,13 +583,19 @@ def main():
                 "h2d_bytes_per_step": q.numel() * q.element_size() +
                 (kv_new.numel() * kv_new.element_size() if owns_last else 0),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
-                "step": "H2D q, k_new, v_new (pinned) -> append k, v to the int8 cache -> "
-                        "decode -> D2H O -> host sync"},
+                "step": "H2D q, k_new, v_new (pinned) -> " +
+                        ("append k, v to the int8 cache (separate launches) -> decode"
+                         if collective and not use_p2p else
+                         "decode with the append of k, v fused in (tqkv_decode_int8_append)") +
+                        (" -> exchange + combine" if collective else "") + " -> D2H O -> host sync"},
         "gpu_launches": args.steps * (2 if collective else 1),
         "clocks": clk.summary(),
         "compress": {"us_per_tensor": statistics.mean(comp_us),
                      "GBps": (w.BH * S_loc * w.D * 3 + w.BH * S_loc * (w.D // w.block_size) * 2)
                      / (statistics.mean(comp_us) * 1e-6) / 1e9},
+        "l2_hot": None if flush_buf is None else {
+            "us_per_step": hot_ms * 1e3, "GBps": total_bytes / (hot_ms * 1e-3) / 1e9,
+            "note": "same steps back to back, KV resident in L2"},
         "device_error": int(err_max),
         "kernels": kernels,
     }

@@ -97,9 +97,10 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
 /* ------------------------------------------------------------------------ */
 /* Decode attention: O[b,h,:] = softmax(q . K^T / sqrt(D)) . V per (b, h).
  *
- * The work of all B*H heads is cut into equal runs of token rows, one run per
- * CTA; a head that spans several CTAs is merged by the last CTA to finish it
- * (log-sum-exp), using `workspace`.  Size the workspace with
+ * The B*H*S token rows are cut into fixed chunks that the CTAs claim from a
+ * counter in `workspace`; a head that spans several chunks is merged by the
+ * chunk that finishes it last (log-sum-exp), also in `workspace`.  Size the
+ * workspace with
  * tqkv_decode_workspace_bytes() and zero it once with tqkv_workspace_init()
  * before its first use; every decode call leaves it zeroed again.  Calls that
  * share one workspace must be ordered (same stream, or events).
@@ -135,6 +136,25 @@ tqkv_status tqkv_decode_int8_cache(const void* q,
                                    int B, int H, int S, int S_cap, int D, int block_size,
                                    void* workspace, size_t workspace_bytes,
                                    cudaStream_t stream);
+
+/* Append fused into decode (no counterpart in the reference, whose drivers
+ * compress whole tensors and then attend).  Equivalent to
+ *   tqkv_kv_append(k_new, kq, ks, B, H, T, D, block_size, S_cap, S - T);
+ *   tqkv_kv_append(v_new, vq, vs, ...same...);
+ *   tqkv_decode_int8_cache(q, kq, ks, vq, vs, o, B, H, S, S_cap, D, ...);
+ * in one launch: the T newest tokens of each head, k_new / v_new fp16
+ * [B, H, T, D], are quantised (same codes and scales as tqkv_kv_compress) by
+ * the CTA whose tile holds them, written to rows [S - T, S) of the caches and
+ * attended from shared memory without being read back.  Rows [0, S - T) must
+ * already hold codes.  Requires 1 <= T <= S <= S_cap; k_new, v_new, kq and vq
+ * 16-byte aligned.  Workspace as for tqkv_decode_int8 with the same B, H, S, D. */
+tqkv_status tqkv_decode_int8_append(const void* q, const void* k_new, const void* v_new,
+                                    int8_t* kq, void* ks, int8_t* vq, void* vs,
+                                    void* o,
+                                    int B, int H, int T, int S, int S_cap, int D,
+                                    int block_size,
+                                    void* workspace, size_t workspace_bytes,
+                                    cudaStream_t stream);
 
 /* FP16 decode attention on the same split-S skeleton.
  * Replaces launch_decode_attn_baseline (reference include/attention.h:6-12,
@@ -204,6 +224,17 @@ tqkv_status tqkv_decode_int8_publish(const void* q,
                                      void* workspace, size_t workspace_bytes,
                                      void* const* exchange_bufs, int world, int rank,
                                      cudaStream_t stream);
+/* tqkv_decode_int8_publish with the fused append of tqkv_decode_int8_append:
+ * the rank that holds the end of the sequence appends the T newest tokens
+ * at rows [S - T, S) of its slice (a cache of S_cap rows per head). */
+tqkv_status tqkv_decode_int8_append_publish(const void* q,
+                                            const void* k_new, const void* v_new,
+                                            int8_t* kq, void* ks, int8_t* vq, void* vs,
+                                            int B, int H, int T, int S, int S_cap, int D,
+                                            int block_size,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* const* exchange_bufs, int world, int rank,
+                                            cudaStream_t stream);
 tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o,
                                   int world, int rank, int BH, int D, cudaStream_t stream);
 

@@ -49,6 +49,7 @@
 #include <cuda_fp16.h>
 
 #include "device_common.cuh"
+#include "kv_compress.cuh"
 
 namespace tqkv {
 
@@ -117,6 +118,9 @@ struct DecodeArgs {
     int max_parts;
     float score_scale_log2;    // log2(e) / sqrt(D)
     PeerArgs peer;             // kOutPeers only
+    const void* k_new;         // fused append only: fp16 [BH][T_new][D], rows [S - T_new, S)
+    const void* v_new;
+    int T_new;
 };
 
 template <int D, int BS, bool kHalfKV>
@@ -266,12 +270,67 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) {
 }
 
 // ---------------------------------------------------------------------------
-// Producer: one lane streams every tile of this CTA's run into the ring.
-template <int D, int BS, bool kHalfKV>
+// Fused append: the newest T rows of every head (rows [S - T, S)) are not yet
+// in the cache; the producer warp quantises them from fp16 (k_new / v_new
+// [BH][T][D]), writes codes and scales to the cache and into the tile's
+// shared-memory slots, and the bulk copies cover only the older rows.
+constexpr int kNoAppend = -1;
+
+// Tile rows [n0, n1) (relative to the tile start t0, memory row row0) are new
+// tokens.  Lanes [0, D/8) quantise the K row, lanes [D/8, D/4) the V row, with
+// the same rounding as the compress kernel (division form MODE).
+template <int D, int BS, int MODE>
+__device__ __forceinline__ void append_rows(const DecodeArgs& a, uint8_t* st, int bh, int t0,
+                                            int n0, int n1, long long row0, int ks_off,
+                                            int vs_off) {
+    using C = DecodeCfg<D, BS, false>;
+    constexpr int kLPR = D / 8;  // lanes per row, 8 values each
+    constexpr int kLPB = BS / 8;
+    constexpr int kNSub = D / BS;
+    const int lane = threadIdx.x & 31;
+    const int tensor = lane / kLPR;  // 0: K, 1: V, 2..3: idle (D = 64)
+    const int c = lane % kLPR;
+    const bool active = tensor < 2;
+    const uint4* src = static_cast<const uint4*>(tensor == 0 ? a.k_new : a.v_new);
+    uint2* cache_q = static_cast<uint2*>(const_cast<void*>(tensor == 0 ? a.k : a.v));
+    __half* cache_s = reinterpret_cast<__half*>(const_cast<uint16_t*>(tensor == 0 ? a.ks : a.vs));
+    const int off_q = tensor == 0 ? C::kOffK : C::kOffV;
+    const int off_s = tensor == 0 ? C::kOffKS + ks_off : C::kOffVS + vs_off;
+    const int first_new = a.S - a.T_new;
+    for (int t = n0; t < n1; ++t) {
+        const long long j = static_cast<long long>(bh) * a.T_new + (t0 + t - first_new);
+        const uint4 raw = active ? __ldg(src + j * kLPR + c) : make_uint4(0u, 0u, 0u, 0u);
+        __half sc;
+        const uint2 codes = quantize_lane<BS, MODE>(raw, sc);
+        if (active) {
+            const long long mrow = row0 + t;
+            *reinterpret_cast<uint2*>(st + off_q + t * C::kRowBytes + c * 8) = codes;
+            cache_q[mrow * kLPR + c] = codes;
+            if (c % kLPB == 0) {
+                *reinterpret_cast<__half*>(st + off_s + (t * kNSub + c / kLPB) * 2) = sc;
+                cache_s[mrow * kNSub + c / kLPB] = sc;
+            }
+        }
+    }
+}
+
+template <bool kWarp>
+__device__ __forceinline__ unsigned int warp_bcast(unsigned int v) {
+    if constexpr (kWarp) return __shfl_sync(0xffffffffu, v, 0);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Producer: streams every tile of the chunks this CTA claims into the ring.
+// One lane, or (fused append) the whole warp, with lane 0 issuing the copies.
+template <int D, int BS, bool kHalfKV, int APPEND>
 __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* smem,
                                                 uint64_t* full, uint64_t* empty,
                                                 TileMeta* meta, CtaCtl* ctl) {
     using C = DecodeCfg<D, BS, kHalfKV>;
+    constexpr bool kWarp = APPEND != kNoAppend;
+    static_assert(!(kWarp && kHalfKV), "fused append is INT8 only");
+    const bool leader = !kWarp || (threadIdx.x & 31) == 0;
     const uint64_t policy = make_evict_first_policy();
     const uint64_t q_lo = reinterpret_cast<uint64_t>(a.q);
     const uint64_t q_hi = q_lo + static_cast<uint64_t>(a.BH) * D * 2;
@@ -280,6 +339,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     const uint64_t sc_bytes = static_cast<uint64_t>(a.BH) * a.S_stride * C::kNSub * 2;
     const uint8_t* kbase = static_cast<const uint8_t*>(a.k);
     const uint8_t* vbase = static_cast<const uint8_t*>(a.v);
+    const int first_new = kWarp ? a.S - a.T_new : a.S;  // rows >= first_new are appended
 
     int stage = 0;
     uint32_t phase = 0;
@@ -290,9 +350,10 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     // of a split head (and their indices) deterministic.
     unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
     while (ok) {
-        unsigned int chunk;
+        unsigned int chunk = 0;
         if (a.sched != nullptr) {
-            chunk = atomicAdd(&a.sched[0], 1u);
+            if (leader) chunk = atomicAdd(&a.sched[0], 1u);
+            chunk = warp_bcast<kWarp>(chunk);
         } else {
             chunk = static_chunk;
             static_chunk += gridDim.x;
@@ -309,70 +370,95 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             const long long u_last = (head0 + a.S - 1) / a.chunk_rows;
             for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
                 const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
-                if (ld_volatile_shared(&ctl->abort)) {
-                    ok = false;
-                    break;
+                unsigned int got = 0;  // 0: stage free, 1: aborted, 2: wait gave up
+                if (leader) {
+                    if (ld_volatile_shared(&ctl->abort)) {
+                        got = 1;
+                    } else if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+                        record_device_error(kErrEmptyWaitTimeout);
+                        atomicExch(&ctl->abort, 1u);
+                        got = 2;
+                    }
                 }
-                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
-                    record_device_error(kErrEmptyWaitTimeout);
-                    atomicExch(&ctl->abort, 1u);
+                if (warp_bcast<kWarp>(got) != 0u) {
                     ok = false;
                     break;
                 }
                 uint8_t* st = smem + stage * C::kStageBytes;
                 const long long row0 = static_cast<long long>(bh) * a.S_stride + t0;  // memory row
-                const uint32_t kv_bytes = static_cast<uint32_t>(cnt) * C::kRowBytes;
-                uint32_t tx = 2 * kv_bytes;
+                // rows [0, nb) of the tile come from the cache, [nb, cnt) are new
+                int nb = first_new - t0;
+                nb = nb < 0 ? 0 : (nb > cnt ? cnt : nb);
+                const uint64_t ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                const uint64_t vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
+                if constexpr (kWarp) {
+                    // nb is warp-uniform; a tile without new rows needs no
+                    // warp barrier (and no fence that could wait on earlier
+                    // memory operations of the leader)
+                    if (nb < cnt) {
+                        append_rows<D, BS, APPEND>(a, st, bh, t0, nb, cnt, row0,
+                                                   static_cast<int>(ks_src & 15),
+                                                   static_cast<int>(vs_src & 15));
+                        __syncwarp();  // orders the lanes' shared stores before the arrive
+                    }
+                }
+                if (leader) {
+                    const uint32_t kv_bytes = static_cast<uint32_t>(nb) * C::kRowBytes;
+                    uint32_t tx = 2 * kv_bytes;
 
-                TileMeta& m = meta[stage];
-                m.bh = bh;
-                m.t0 = t0;
-                m.cnt = cnt;
-                m.flags = (t0 == t_a ? kTileFirst : 0) | (t0 + C::kTile >= t_b ? kTileLast : 0);
-                m.part = static_cast<int>(chunk - u_first);
-                m.nparts = static_cast<int>(u_last - u_first + 1);
+                    TileMeta& m = meta[stage];
+                    m.bh = bh;
+                    m.t0 = t0;
+                    m.cnt = cnt;
+                    m.flags = (t0 == t_a ? kTileFirst : 0) | (t0 + C::kTile >= t_b ? kTileLast : 0);
+                    m.part = static_cast<int>(chunk - u_first);
+                    m.nparts = static_cast<int>(u_last - u_first + 1);
 
-                Span sk{}, sv{}, sq{};
-                uint64_t ks_src = 0, vs_src = 0, q_src = 0;
-                uint32_t sc_n = 0;
-                if constexpr (!kHalfKV) {
-                    sc_n = static_cast<uint32_t>(cnt) * C::kNSub * 2;
-                    ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
-                    vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
-                    sk = plan_span(ks_src, sc_n, ks_lo, ks_lo + sc_bytes);
-                    sv = plan_span(vs_src, sc_n, vs_lo, vs_lo + sc_bytes);
-                    tx += sk.bulk_bytes + sv.bulk_bytes;
-                    copy_span_edges(st + C::kOffKS, ks_src, sc_n, sk);
-                    copy_span_edges(st + C::kOffVS, vs_src, sc_n, sv);
-                }
-                const bool first = (t0 == t_a);
-                if (first) {
-                    q_src = q_lo + static_cast<uint64_t>(bh) * D * 2;
-                    sq = plan_span(q_src, D * 2, q_lo, q_hi);
-                    tx += sq.bulk_bytes;
-                    copy_span_edges(st + C::kOffQ, q_src, D * 2, sq);
-                }
-                mbar_arrive_expect_tx(&full[stage], tx);
-                bulk_copy_g2s(st + C::kOffK, kbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
-                              policy);
-                bulk_copy_g2s(st + C::kOffV, vbase + row0 * C::kRowBytes, kv_bytes, &full[stage],
-                              policy);
-                if constexpr (!kHalfKV) {
-                    if (sk.bulk_bytes)
-                        bulk_copy_g2s(st + C::kOffKS + sk.bulk_dst_off,
-                                      reinterpret_cast<const void*>(sk.bulk_src), sk.bulk_bytes,
+                    Span sk{}, sv{}, sq{};
+                    uint64_t q_src = 0;
+                    if constexpr (!kHalfKV) {
+                        const uint32_t sc_n = static_cast<uint32_t>(nb) * C::kNSub * 2;
+                        // with appended rows the bulk span must stop short of their
+                        // scales, which the warp has written into the same slot
+                        const uint64_t k_hi = nb < cnt ? ks_src + sc_n : ks_lo + sc_bytes;
+                        const uint64_t v_hi = nb < cnt ? vs_src + sc_n : vs_lo + sc_bytes;
+                        sk = plan_span(ks_src, sc_n, ks_lo, k_hi);
+                        sv = plan_span(vs_src, sc_n, vs_lo, v_hi);
+                        tx += sk.bulk_bytes + sv.bulk_bytes;
+                        copy_span_edges(st + C::kOffKS, ks_src, sc_n, sk);
+                        copy_span_edges(st + C::kOffVS, vs_src, sc_n, sv);
+                    }
+                    const bool first = (t0 == t_a);
+                    if (first) {
+                        q_src = q_lo + static_cast<uint64_t>(bh) * D * 2;
+                        sq = plan_span(q_src, D * 2, q_lo, q_hi);
+                        tx += sq.bulk_bytes;
+                        copy_span_edges(st + C::kOffQ, q_src, D * 2, sq);
+                    }
+                    mbar_arrive_expect_tx(&full[stage], tx);
+                    if (kv_bytes) {
+                        bulk_copy_g2s(st + C::kOffK, kbase + row0 * C::kRowBytes, kv_bytes,
                                       &full[stage], policy);
-                    if (sv.bulk_bytes)
-                        bulk_copy_g2s(st + C::kOffVS + sv.bulk_dst_off,
-                                      reinterpret_cast<const void*>(sv.bulk_src), sv.bulk_bytes,
+                        bulk_copy_g2s(st + C::kOffV, vbase + row0 * C::kRowBytes, kv_bytes,
                                       &full[stage], policy);
+                    }
+                    if constexpr (!kHalfKV) {
+                        if (sk.bulk_bytes)
+                            bulk_copy_g2s(st + C::kOffKS + sk.bulk_dst_off,
+                                          reinterpret_cast<const void*>(sk.bulk_src), sk.bulk_bytes,
+                                          &full[stage], policy);
+                        if (sv.bulk_bytes)
+                            bulk_copy_g2s(st + C::kOffVS + sv.bulk_dst_off,
+                                          reinterpret_cast<const void*>(sv.bulk_src), sv.bulk_bytes,
+                                          &full[stage], policy);
+                    }
+                    if (first && sq.bulk_bytes) {
+                        bulk_copy_g2s(st + C::kOffQ + sq.bulk_dst_off,
+                                      reinterpret_cast<const void*>(sq.bulk_src), sq.bulk_bytes,
+                                      &full[stage], policy);
+                    }
+                    ++issued;
                 }
-                if (first && sq.bulk_bytes) {
-                    bulk_copy_g2s(st + C::kOffQ + sq.bulk_dst_off,
-                                  reinterpret_cast<const void*>(sq.bulk_src), sq.bulk_bytes,
-                                  &full[stage], policy);
-                }
-                ++issued;
                 if (++stage == kDecodeStages) {
                     stage = 0;
                     phase ^= 1u;
@@ -381,6 +467,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             r = head0 + t_b;
         }
     }
+    if (!leader) return;
     // end-of-work marker for the consumers
     if (ok) {
         if (mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
@@ -894,7 +981,7 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
 // ---------------------------------------------------------------------------
 constexpr int kDecodeCtasPerSm = 4;  // target residency (smem: 3 stages; regs: <= 102 per thread)
 
-template <int D, int BS, bool kHalfKV, int OUT>
+template <int D, int BS, bool kHalfKV, int OUT, int APPEND = kNoAppend>
 __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     decode_attn_kernel(const DecodeArgs a) {
     using C = DecodeCfg<D, BS, kHalfKV>;
@@ -920,7 +1007,8 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
 
     const int warp = threadIdx.x >> 5;
     if (warp == kDecodeConsumerWarps) {
-        if ((threadIdx.x & 31) == 0) decode_producer<D, BS, kHalfKV>(a, smem, full, empty, meta, ctl);
+        if (APPEND != kNoAppend || (threadIdx.x & 31) == 0)
+            decode_producer<D, BS, kHalfKV, APPEND>(a, smem, full, empty, meta, ctl);
         return;
     }
 

@@ -75,17 +75,13 @@ __device__ __forceinline__ void st_stream_v4(uint4* p, uint4 v) {
                  : "memory");
 }
 
-// Quantise the 8 fp16 values in `raw` (lane c of a row) and store codes and,
-// on the first lane of each block, the block's fp16 scale.
-template <int D, int BS, int MODE>
-__device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool valid, int c,
-                                              uint2* __restrict__ xq,
-                                              __half* __restrict__ scales) {
-    // `row` is the destination row of codes and scales
-    constexpr int kLPR = D / 8;   // lanes per row
+// Quantise the 8 fp16 values in `raw` (one lane's share of a row): returns
+// their codes (8 bytes) and sets `scale` to the fp16 scale of the lane's
+// block.  The block max is a shuffle over aligned groups of BS/8 lanes, so
+// every lane of the warp must call it.
+template <int BS, int MODE>
+__device__ __forceinline__ uint2 quantize_lane(uint4 raw, __half& scale) {
     constexpr int kLPB = BS / 8;  // lanes per block
-    constexpr int kNSub = D / BS;
-
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
     float f[8];
 #pragma unroll
@@ -104,10 +100,7 @@ __device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool val
 
     float s = kv_div<MODE>(a, 127.0f);
     if (s == 0.0f) s = 1.0f;
-
-    if (valid && (c % kLPB) == 0) {
-        scales[row * kNSub + c / kLPB] = __float2half_rn(s);
-    }
+    scale = __float2half_rn(s);
 
     uint32_t packed[2];
 #pragma unroll
@@ -122,9 +115,23 @@ __device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool val
         }
         packed[h] = word;
     }
-    if (valid) {
-        st_stream_v2(xq + row * kLPR + c, make_uint2(packed[0], packed[1]));
-    }
+    return make_uint2(packed[0], packed[1]);
+}
+
+// Quantise lane c's 8 values of a row and store its codes and, on the first
+// lane of each block, the block's fp16 scale.
+template <int D, int BS, int MODE>
+__device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool valid, int c,
+                                              uint2* __restrict__ xq,
+                                              __half* __restrict__ scales) {
+    // `row` is the destination row of codes and scales
+    constexpr int kLPR = D / 8;   // lanes per row
+    constexpr int kLPB = BS / 8;  // lanes per block
+    constexpr int kNSub = D / BS;
+    __half scale;
+    const uint2 codes = quantize_lane<BS, MODE>(raw, scale);
+    if (valid && (c % kLPB) == 0) scales[row * kNSub + c / kLPB] = scale;
+    if (valid) st_stream_v2(xq + row * kLPR + c, codes);
 }
 
 // Destination row of source row `r` when T rows per head are written at rows
@@ -171,7 +178,9 @@ __global__ void __launch_bounds__(kCompressThreads)
 // Kernel B: y = fp16(float(code) * float(scale)).  The product of a 7-bit
 // code and an 11-bit scale is exact in fp32, so the only rounding is the
 // final fp16 conversion, as in the reference (src/kv_reconstruct.cu:33).
-// One lane owns 16 codes (one 16-byte load, two 16-byte stores).
+// One lane owns 16 codes (one 16-byte load, two 16-byte stores); each warp
+// step loads kCompressUnroll row groups before converting any of them, so that
+// several loads per lane are in flight.
 template <int D, int BS>
 __global__ void __launch_bounds__(kCompressThreads)
     kv_reconstruct_kernel(const uint4* __restrict__ xq, const __half* __restrict__ scales,
@@ -179,32 +188,47 @@ __global__ void __launch_bounds__(kCompressThreads)
     constexpr int kLPR = D / 16;
     constexpr int kRPW = 32 / kLPR;
     constexpr int kNSub = D / BS;
+    constexpr int kU = kCompressUnroll;
     const int lane = threadIdx.x & 31;
     const int c = lane % kLPR;
     const int rsub = lane / kLPR;
     const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
-    for (long long r0 = warp * kRPW; r0 < rows; r0 += nwarps * kRPW) {
-        const long long row = r0 + rsub;
-        if (row >= rows) continue;
-        const uint4 raw = ld_stream_v4(xq + row * kLPR + c);
-        const float s = __half2float(scales[row * kNSub + (16 * c) / BS]);
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-        uint32_t out[8];
+    for (long long r0 = warp * (kU * kRPW); r0 < rows; r0 += nwarps * (kU * kRPW)) {
+        uint4 raw[kU];
+        __half sh[kU];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const int lo = static_cast<int8_t>((w[i] >> (16 * p)) & 0xffu);
-                const int hi = static_cast<int8_t>((w[i] >> (16 * p + 8)) & 0xffu);
-                const __half2 h = __halves2half2(__float2half_rn(static_cast<float>(lo) * s),
-                                                 __float2half_rn(static_cast<float>(hi) * s));
-                out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int u = 0; u < kU; ++u) {
+            const long long row = r0 + u * kRPW + rsub;
+            raw[u] = make_uint4(0, 0, 0, 0);
+            sh[u] = __ushort_as_half(0);
+            if (row < rows) {
+                raw[u] = ld_stream_v4(xq + row * kLPR + c);
+                sh[u] = scales[row * kNSub + (16 * c) / BS];
             }
         }
-        st_stream_v4(y + (row * kLPR + c) * 2, make_uint4(out[0], out[1], out[2], out[3]));
-        st_stream_v4(y + (row * kLPR + c) * 2 + 1, make_uint4(out[4], out[5], out[6], out[7]));
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const long long row = r0 + u * kRPW + rsub;
+            if (row >= rows) continue;
+            const float s = __half2float(sh[u]);
+            const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+            uint32_t out[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    const int lo = static_cast<int8_t>((w[i] >> (16 * p)) & 0xffu);
+                    const int hi = static_cast<int8_t>((w[i] >> (16 * p + 8)) & 0xffu);
+                    const __half2 h = __halves2half2(__float2half_rn(static_cast<float>(lo) * s),
+                                                     __float2half_rn(static_cast<float>(hi) * s));
+                    out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+            }
+            st_stream_v4(y + (row * kLPR + c) * 2, make_uint4(out[0], out[1], out[2], out[3]));
+            st_stream_v4(y + (row * kLPR + c) * 2 + 1, make_uint4(out[4], out[5], out[6], out[7]));
+        }
     }
 }
 

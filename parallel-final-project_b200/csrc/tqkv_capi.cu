@@ -42,6 +42,10 @@ thread_local int t_last_cuda_error = 0;
 constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipeline fill
 constexpr long long kChunksPerCta = 8;     // scheduling chunks per CTA (load balance)
 constexpr long long kChunkAlign = 128;     // chunk rows: a multiple of every tile height
+// Below this many rows per CTA every CTA takes one run of rows, statically:
+// the runs are short, so a chunk claim and a split-head merge per chunk
+// would cost more than the imbalance they remove.
+constexpr long long kMinDynamicRowsPerCta = 2048;
 constexpr int kMaxCtasPerSmBound = 4;      // >= any decode kernel's occupancy (smem-bound)
 
 struct KernelKey {
@@ -94,20 +98,23 @@ struct DecodePlan {
     int max_parts;
 };
 
-// Rows are cut into fixed chunks of C rows that the CTAs claim dynamically,
-// about kChunksPerCta per CTA, so SMs that stream faster take more chunks.
-// `max_ctas` caps the grid (resident CTAs).  One CTA takes everything as one
-// chunk.  C does not grow with max_ctas, so a bound plan computed with the
-// largest grid has the most parts per head.
+// Rows are cut into fixed chunks of C rows.  With many rows per CTA there are
+// about kChunksPerCta chunks per CTA, claimed dynamically, so SMs that stream
+// faster take more of them; otherwise one chunk per CTA (a static run, C
+// rounded to 16 rows).  `max_ctas` caps the grid (resident CTAs).  C does not
+// grow with max_ctas, so a bound plan computed with the largest grid has the
+// most parts per head.
 DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
     DecodePlan p{};
     long long g = (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta;
     if (g > max_ctas) g = max_ctas;
     if (g < 1) g = 1;
-    long long c = total_rows;
-    if (g > 1) {
+    long long c = (total_rows + g - 1) / g;
+    if (c >= kMinDynamicRowsPerCta) {
         c = (total_rows + g * kChunksPerCta - 1) / (g * kChunksPerCta);
         c = (c + kChunkAlign - 1) / kChunkAlign * kChunkAlign;
+    } else if (g > 1) {
+        c = (c + 15) / 16 * 16;
     }
     p.chunk_rows = c;
     p.nchunks = (total_rows + c - 1) / c;
@@ -116,11 +123,17 @@ DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
     return p;
 }
 
-// The workspace layout is fixed by an upper bound on the grid so that its
-// size does not depend on which decode kernel runs.
+// The workspace layout is fixed by an upper bound on the parts per head over
+// every grid cap a decode kernel can have (SMs x 1..kMaxCtasPerSmBound
+// resident CTAs), so that its size does not depend on which kernel runs.
 DecodePlan bound_plan(long long total_rows, int S, int device) {
-    const long long cap = static_cast<long long>(sm_count(device)) * kMaxCtasPerSmBound;
-    return make_plan(total_rows, S, cap > 0 ? cap : 1);
+    const long long sms = sm_count(device) > 0 ? sm_count(device) : 1;
+    DecodePlan b = make_plan(total_rows, S, sms);
+    for (long long occ = 2; occ <= kMaxCtasPerSmBound; ++occ) {
+        const DecodePlan p = make_plan(total_rows, S, sms * occ);
+        if (p.max_parts > b.max_parts) b = p;
+    }
+    return b;
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -188,7 +201,7 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
     if (e != cudaSuccess) return from_cuda(e);
     auto fn = kv_reconstruct_kernel<D, BS>;
     const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
-    const long long rows_per_block = (kCompressThreads / 32) * (32 / (D / 16));
+    const long long rows_per_block = (kCompressThreads / 32) * (32 / (D / 16)) * kCompressUnroll;
     long long grid = (rows + rows_per_block - 1) / rows_per_block;
     const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
     if (grid > cap) grid = cap;
@@ -199,7 +212,7 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
                                    rows));
 }
 
-template <int D, int BS, bool kHalfKV, int OUT>
+template <int D, int BS, bool kHalfKV, int OUT, int APPEND = kNoAppend>
 tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void* workspace,
                         size_t workspace_bytes, cudaStream_t stream) {
     // a.peer is set by the caller (kOutPeers) or zero; a.S_stride by the caller
@@ -207,7 +220,7 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return from_cuda(e);
-    auto fn = decode_attn_kernel<D, BS, kHalfKV, OUT>;
+    auto fn = decode_attn_kernel<D, BS, kHalfKV, OUT, APPEND>;
     const int per_sm = prepare_kernel(fn, kDecodeThreads, C::kSmemBytes, dev);
     if (per_sm <= 0) return from_cuda(cudaErrorInvalidConfiguration);
 
@@ -220,7 +233,9 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    a.sched = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.sched_off) : nullptr;
+    // one chunk per CTA: no claims, chunk = blockIdx.x
+    a.sched = plan.nchunks > plan.grid ? reinterpret_cast<unsigned int*>(ws + lay.sched_off)
+                                        : nullptr;
     a.tickets = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.tickets_off) : nullptr;
     a.parts = needs_ws ? reinterpret_cast<float*>(ws + lay.parts_off) : nullptr;
     a.total_rows = total_rows;
@@ -237,6 +252,15 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
 template <int D, int BS, bool kHalfKV>
 tqkv_status decode_out(OutKind out, const DecodeArgs& a, long long total, int S, int BH,
                        void* ws, size_t wsb, cudaStream_t stream) {
+    if constexpr (!kHalfKV) {
+        // fused append: quantise the newest rows with the compress kernel's rounding
+        constexpr int kAppend = TQKV_COMPRESS_DIV_MODE;
+        if (a.T_new > 0 && out == OutKind::kHalfO)
+            return decode_impl<D, BS, false, kOutHalf, kAppend>(a, total, S, BH, ws, wsb, stream);
+        if (a.T_new > 0 && out == OutKind::kPeers)
+            return decode_impl<D, BS, false, kOutPeers, kAppend>(a, total, S, BH, ws, wsb, stream);
+    }
+    if (a.T_new > 0) return TQKV_ERR_UNSUPPORTED;
     if (out == OutKind::kHalfO)
         return decode_impl<D, BS, kHalfKV, kOutHalf>(a, total, S, BH, ws, wsb, stream);
     if (out == OutKind::kPartial)
@@ -249,7 +273,8 @@ tqkv_status decode_out(OutKind out, const DecodeArgs& a, long long total, int S,
 // INT8 decode with the kOutPeers epilogue (split-S over NVLink).
 tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void* k, const void* ks,
                                 const void* v, const void* vs, int BH, int S, int D, int bs,
-                                void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                                int S_stride = 0, const AppendRows* append = nullptr) {
     DecodeArgs a{};
     a.q = q;
     a.k = k;
@@ -258,7 +283,12 @@ tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void*
     a.vs = static_cast<const uint16_t*>(vs);
     a.out = nullptr;
     a.peer = peer;
-    a.S_stride = S;
+    a.S_stride = S_stride > 0 ? S_stride : S;
+    if (append != nullptr) {
+        a.k_new = append->k_new;
+        a.v_new = append->v_new;
+        a.T_new = append->T;
+    }
     const long long total = static_cast<long long>(BH) * S;
     const OutKind o = OutKind::kPeers;
     if (D == 64 && bs == 32) return decode_out<64, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
@@ -341,9 +371,15 @@ tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, lo
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D, int bs,
                           void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                          int S_stride) {
+                          int S_stride, const AppendRows* append) {
     DecodeArgs a{};
     a.S_stride = S_stride > 0 ? S_stride : S;
+    if (append != nullptr) {
+        if (kv != KvKind::kInt8) return TQKV_ERR_UNSUPPORTED;
+        a.k_new = append->k_new;
+        a.v_new = append->v_new;
+        a.T_new = append->T;
+    }
     a.q = q;
     a.k = k;
     a.v = v;
@@ -518,6 +554,24 @@ tqkv_status tqkv_decode_int8_cache(const void* q, const int8_t* kq, const void* 
                                stream, S_cap);
 }
 
+tqkv_status tqkv_decode_int8_append(const void* q, const void* k_new, const void* v_new,
+                                    int8_t* kq, void* ks, int8_t* vq, void* vs, void* o, int B,
+                                    int H, int T, int S, int S_cap, int D, int block_size,
+                                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || T <= 0 || S < T || S_cap < S) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o || !k_new || !v_new || !kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq) || !tqkv::aligned16(k_new) ||
+        !tqkv::aligned16(v_new))
+        return TQKV_ERR_MISALIGNED;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    const tqkv::AppendRows rows{k_new, v_new, T};
+    return tqkv::launch_decode(KvKind::kInt8, OutKind::kHalfO, q, kq, ks, vq, vs, o,
+                               static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
+                               stream, S_cap, &rows);
+}
+
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D) {
     if (B <= 0 || H <= 0 || S <= 0 || (D != 64 && D != 128)) return 0;
     return tqkv::decode_workspace_bytes(static_cast<long long>(B) * H, S, D);
@@ -671,6 +725,30 @@ tqkv_status tqkv_decode_int8_publish(const void* q, const int8_t* kq, const void
     if (pst != TQKV_OK) return pst;
     return tqkv::launch_decode_peers(peer, q, kq, ks, vq, vs, static_cast<int>(BH), S, D,
                                      block_size, workspace, workspace_bytes, stream);
+}
+
+tqkv_status tqkv_decode_int8_append_publish(const void* q, const void* k_new, const void* v_new,
+                                            int8_t* kq, void* ks, int8_t* vq, void* vs, int B,
+                                            int H, int T, int S, int S_cap, int D, int block_size,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* const* exchange_bufs, int world, int rank,
+                                            cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || T <= 0 || S < T || S_cap < S || world <= 0 ||
+        world > tqkv::kMaxPeers || rank < 0 || rank >= world)
+        return TQKV_ERR_INVALID_SIZE;
+    if (!q || !k_new || !v_new || !kq || !ks || !vq || !vs || !exchange_bufs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq) || !tqkv::aligned16(k_new) ||
+        !tqkv::aligned16(v_new))
+        return TQKV_ERR_MISALIGNED;
+    const long long BH = static_cast<long long>(B) * H;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    tqkv::PeerArgs peer{};
+    const tqkv_status pst = tqkv::make_peer_args(exchange_bufs, world, rank, &peer);
+    if (pst != TQKV_OK) return pst;
+    const tqkv::AppendRows rows{k_new, v_new, T};
+    return tqkv::launch_decode_peers(peer, q, kq, ks, vq, vs, static_cast<int>(BH), S, D,
+                                     block_size, workspace, workspace_bytes, stream, S_cap, &rows);
 }
 
 tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o, int world, int rank,

@@ -27,11 +27,22 @@ tqkv_status launch_compress(const void* x, int8_t* xq, void* scales, long long r
                             int t0 = 0);
 tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, long long rows,
                                int D, int block_size, cudaStream_t stream);
+// The newest T rows of every head, given in fp16 ([BH][T][D] each), that a
+// fused decode quantises into rows [S - T, S) of the INT8 cache before
+// attending over them.
+struct AppendRows {
+    const void* k_new;
+    const void* v_new;
+    int T;
+};
+
 // S rows attended per head; S_stride rows between heads in memory (0: S).
+// With `append`, K/V/scales are the cache the new rows are written into.
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D,
                           int block_size, void* workspace, size_t workspace_bytes,
-                          cudaStream_t stream, int S_stride = 0);
+                          cudaStream_t stream, int S_stride = 0,
+                          const AppendRows* append = nullptr);
 tqkv_status launch_fill_half(void* o, long long n, uint16_t bits, cudaStream_t stream);
 tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t stream);
 

@@ -96,6 +96,28 @@ def decode_int8_cache(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: t
     return out
 
 
+def decode_int8_append(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                       kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor, vs: torch.Tensor,
+                       S: int, block_size: int, out: Optional[torch.Tensor] = None,
+                       workspace: Optional["Workspace"] = None, stream=None) -> torch.Tensor:
+    """Append fused into decode: quantise the T newest tokens (k_new / v_new fp16
+    [B,H,T,D]) into rows [S-T, S) of the caches (kq/vq int8 [B,H,S_cap,D], ks/vs
+    fp16 [B,H,S_cap,D/bs]) and attend over rows [0, S), in one launch."""
+    B, H, S_cap, D = _bhsd(kq, "kq")
+    T = _bhsd(k_new, "k_new")[2]
+    if k_new.dtype != _F16 or v_new.dtype != _F16 or v_new.shape != k_new.shape:
+        raise ValueError("k_new and v_new must be fp16 [B, H, T, D]")
+    if out is None:
+        out = torch.empty((B, H, D), dtype=_F16, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H, S, D) if S > 0 else 0, stream)
+    lib = load()
+    check("tqkv_decode_int8_append", lib.tqkv_decode_int8_append(
+        _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(kq), _ptr(ks), _ptr(vq), _ptr(vs), _ptr(out),
+        B, H, T, S, S_cap, D, block_size, wptr, wbytes, _stream_handle(stream)))
+    return out
+
+
 def workspace_bytes(B: int, H: int, S: int, D: int) -> int:
     """Scratch the decode kernels need for this shape on the current device."""
     return int(load().tqkv_decode_workspace_bytes(B, H, S, D))

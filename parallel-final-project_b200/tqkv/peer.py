@@ -65,6 +65,20 @@ class PeerExchange:
             B, H, S, D, block_size, wptr, wbytes, self.bufs, self.world, self.rank,
             _stream_handle(stream)))
 
+    def publish_append(self, q, k_new, v_new, kq, ks, vq, vs, S: int, block_size: int,
+                       workspace: Optional[Workspace] = None, stream=None) -> None:
+        """publish() over the first S rows of caches [B, H, S_cap, D] after
+        appending the T newest tokens (k_new / v_new fp16 [B, H, T, D]) at rows
+        [S - T, S), in the same launch."""
+        B, H, S_cap, D = kq.shape
+        T = k_new.shape[2]
+        ws = _workspace(workspace, q.device)
+        wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
+        check("tqkv_decode_int8_append_publish", load().tqkv_decode_int8_append_publish(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), kq.data_ptr(), ks.data_ptr(),
+            vq.data_ptr(), vs.data_ptr(), B, H, T, S, S_cap, D, block_size, wptr, wbytes,
+            self.bufs, self.world, self.rank, _stream_handle(stream)))
+
     def combine(self, out: torch.Tensor, stream=None) -> torch.Tensor:
         check("tqkv_exchange_combine", load().tqkv_exchange_combine(
             self.bufs, out.data_ptr(), self.world, self.rank, self.BH, self.D,
@@ -102,6 +116,7 @@ class LocalExchange:
         self.bufs = (ctypes.c_void_p * 1)(self.own)
 
     publish = PeerExchange.publish
+    publish_append = PeerExchange.publish_append
     combine = PeerExchange.combine
 
     def close(self) -> None:

@@ -25,3 +25,12 @@ def max_abs(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.max(np.abs(a - b))) if a.size else 0.0
+
+
+def assert_tight(got, ref):
+    """|got - ref| <= 1e-3 + |ref| * 2^-10 elementwise: far inside the
+    reference's 1e-2 check; the second term is one fp16 ulp of the output."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    bad = np.abs(got - ref) > 1e-3 + np.abs(ref) * 2.0 ** -10
+    assert not bad.any(), (np.abs(got - ref)[bad].max(), int(bad.sum()))

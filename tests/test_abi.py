@@ -55,3 +55,20 @@ def test_nothing_else_exported():
     exported = _exported()
     ours = {s for s in exported if s.startswith("tqkv_")} | set(_lib.REF_LAUNCHERS.values())
     assert exported == ours, sorted(exported - ours)[:10]
+
+
+def test_fused_append_argument_checks_need_no_gpu():
+    """tqkv_decode_int8_append validates sizes, pointers and alignment before
+    touching the device (the pointers below are never dereferenced)."""
+    lib = tqkv.load()
+    p = 1 << 20
+
+    def call(T, S, S_cap, k_new=p, D=128, bs=64):
+        return lib.tqkv_decode_int8_append(p, k_new, p, p, p, p, p, p, 1, 2, T, S, S_cap, D, bs,
+                                           None, 0, None)
+    assert call(0, 4, 4) == 2
+    assert call(5, 4, 4) == 2
+    assert call(1, 5, 4) == 2
+    assert call(1, 4, 4, k_new=p + 8) == 3
+    assert call(1, 4, 4, D=96) == 1
+    assert call(1, 4, 4, k_new=None) == 6

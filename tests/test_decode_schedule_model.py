@@ -37,6 +37,7 @@ WARPS = _const("decode_attn.cuh", "kDecodeConsumerWarps")
 MIN_ROWS = _const("tqkv_capi.cu", "kMinRowsPerCta")
 CHUNKS_PER_CTA = _const("tqkv_capi.cu", "kChunksPerCta")
 CHUNK_ALIGN = _const("tqkv_capi.cu", "kChunkAlign")
+MIN_DYNAMIC = _const("tqkv_capi.cu", "kMinDynamicRowsPerCta")
 BOUND_OCC = _const("tqkv_capi.cu", "kMaxCtasPerSmBound")
 SMS = 148
 
@@ -44,10 +45,12 @@ SMS = 148
 def make_plan(total, S, max_ctas):
     """(grid, chunk rows C, number of chunks, max_parts)"""
     g = max(min(-(-total // MIN_ROWS), max_ctas), 1)
-    c = total
-    if g > 1:
+    c = -(-total // g)
+    if c >= MIN_DYNAMIC:
         c = -(-total // (g * CHUNKS_PER_CTA))
         c = -(-c // CHUNK_ALIGN) * CHUNK_ALIGN
+    elif g > 1:
+        c = -(-c // 16) * 16
     n = -(-total // c)
     return min(n, g), c, n, (S - 1) // c + 2
 
@@ -59,7 +62,9 @@ def plan_span(src, n, lo, hi):
     return (blo, blo - a16, bhi - blo) if blo < bhi else (0, 0, 0)
 
 
-def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None):
+def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
+    """T_new > 0: the fused-append variant, whose tiles take rows >= S - T_new
+    from the producer warp instead of the bulk copies."""
     S_stride = S if S_stride is None else S_stride
     elem = 2 if half else 1
     RB = D * elem
@@ -72,7 +77,8 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None):
     qslot = D * 2 + 32
     total = BH * S
     grid, R, nchunks, _ = make_plan(total, S, SMS * occ)
-    _, _, _, maxp = make_plan(total, S, SMS * BOUND_OCC)   # workspace layout bound
+    # workspace layout bound: the most parts per head over every grid cap
+    maxp = max(make_plan(total, S, SMS * o)[3] for o in range(1, BOUND_OCC + 1))
     assert 1 <= grid <= nchunks and nchunks < 2 ** 32
     if nchunks == 1:      # no workspace: every head must be one piece
         assert R >= total
@@ -92,17 +98,31 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None):
             # every tile of small cases; first/last few of big ones
             if len(tiles) > 8:
                 tiles = tiles[:4] + tiles[-4:]
+            if T_new:   # every tile holding new rows, too
+                tiles = sorted(set(tiles) | {t for t in range(ta, tb, TILE)
+                                             if t + TILE > S - T_new})
             for t0 in tiles:
                 cnt = min(TILE, tb - t0)
+                nb = min(max(S - T_new - t0, 0), cnt) if T_new else cnt   # rows from the cache
                 row0 = bh * S_stride + t0      # memory row, as the kernel computes it
                 assert 0 < cnt <= TILE and t0 + cnt <= S
-                assert (kbase + row0 * RB) % 16 == 0 and cnt * RB % 16 == 0
-                assert kbase <= kbase + row0 * RB and kbase + (row0 + cnt) * RB <= k_end
+                assert (kbase + row0 * RB) % 16 == 0 and nb * RB % 16 == 0
+                assert kbase <= kbase + row0 * RB and kbase + (row0 + nb) * RB <= k_end
                 assert cnt * RB <= TILE_BYTES
                 if not half:
-                    n = cnt * nsub * 2
+                    n = nb * nsub * 2
                     src = sbase + row0 * nsub * 2
-                    b_src, b_off, b_n = plan_span(src, n, sbase, s_end)
+                    hi = src + n if nb < cnt else s_end
+                    b_src, b_off, b_n = plan_span(src, n, sbase, hi)
+                    if nb < cnt:
+                        # the bulk copy stops short of the new rows' scales,
+                        # which the producer warp writes into the same slot
+                        assert not b_n or b_off + b_n <= (src & 15) + n
+                        for t in range(nb, cnt):
+                            for j in range(nsub):
+                                o = (src & 15) + (t * nsub + j) * 2
+                                assert o + 2 <= slot
+                                assert sbase <= src + (t * nsub + j) * 2 < s_end
                     if b_n:
                         assert sbase <= b_src and b_src + b_n <= s_end
                         assert b_src % 16 == 0 and b_n % 16 == 0 and b_off % 16 == 0
@@ -157,3 +177,12 @@ def test_stage_layout_fits_four_ctas_per_sm():
     stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (128 * 2 + 32)
     smem = STAGES * stage + WARPS * (128 + 2) * 4 + 2 * STAGES * 8 + STAGES * 32 + 32
     assert 4 * (smem + 1024) <= 228 * 1024, smem
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (128, 32), (64, 64), (64, 32)])
+def test_schedule_in_bounds_with_fused_append(D, bs):
+    """The fused-append variant: new rows [S - T, S) of each head."""
+    for BH, S, S_stride, T in [(2, 1, 1, 1), (3, 65, 80, 3), (6, 129, 200, 7), (2, 64, 64, 64),
+                               (6, 2000, 2048, 130), (3, 20000, 20001, 1), (128, 4096, 4096, 2)]:
+        for offs in ((0, 0), (2, 14), (6, 2)):
+            check(BH, S, D, bs, False, 4, offs, S_stride, T)
