@@ -162,7 +162,9 @@ struct DecodeCfg {
 // mbarrier arrive and read by the consumers after their wait.
 enum TileFlags : int { kTileFirst = 1, kTileLast = 2, kTileDone = 4 };
 struct TileMeta {
-    int bh, t0, cnt, flags, part, nparts, pad0, pad1;
+    int bh, t0, cnt, flags, part, nparts;
+    int n_old;  // rows [0, n_old) came from the cache; [n_old, cnt) are appended (fused append)
+    int pad;
 };
 
 // CTA control block in shared memory: the consumer warps' software barrier
@@ -271,17 +273,19 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) {
 
 // ---------------------------------------------------------------------------
 // Fused append: the newest T rows of every head (rows [S - T, S)) are not yet
-// in the cache; the producer warp quantises them from fp16 (k_new / v_new
-// [BH][T][D]), writes codes and scales to the cache and into the tile's
-// shared-memory slots, and the bulk copies cover only the older rows.
+// in the cache.  The bulk copies of a tile cover only its older rows; the
+// consumer warps quantise the new ones from fp16 (k_new / v_new [BH][T][D]),
+// write codes and scales to the cache and into the tile's shared-memory
+// slots, and meet at a barrier before consuming the tile.
 constexpr int kNoAppend = -1;
 
-// Tile rows [n0, n1) (relative to the tile start t0, memory row row0) are new
-// tokens.  Lanes [0, D/8) quantise the K row, lanes [D/8, D/4) the V row, with
-// the same rounding as the compress kernel (division form MODE).
+// Tile rows n0, n0 + step, ... < n1 (relative to the tile start t0, memory
+// row row0) are new tokens; one warp quantises each.  Lanes [0, D/8) take the
+// K row, lanes [D/8, D/4) the V row, with the compress kernel's rounding
+// (division form MODE).
 template <int D, int BS, int MODE>
 __device__ __forceinline__ void append_rows(const DecodeArgs& a, uint8_t* st, int bh, int t0,
-                                            int n0, int n1, long long row0, int ks_off,
+                                            int n0, int n1, int step, long long row0, int ks_off,
                                             int vs_off) {
     using C = DecodeCfg<D, BS, false>;
     constexpr int kLPR = D / 8;  // lanes per row, 8 values each
@@ -297,7 +301,7 @@ __device__ __forceinline__ void append_rows(const DecodeArgs& a, uint8_t* st, in
     const int off_q = tensor == 0 ? C::kOffK : C::kOffV;
     const int off_s = tensor == 0 ? C::kOffKS + ks_off : C::kOffVS + vs_off;
     const int first_new = a.S - a.T_new;
-    for (int t = n0; t < n1; ++t) {
+    for (int t = n0; t < n1; t += step) {
         const long long j = static_cast<long long>(bh) * a.T_new + (t0 + t - first_new);
         const uint4 raw = active ? __ldg(src + j * kLPR + c) : make_uint4(0u, 0u, 0u, 0u);
         __half sc;
@@ -314,23 +318,16 @@ __device__ __forceinline__ void append_rows(const DecodeArgs& a, uint8_t* st, in
     }
 }
 
-template <bool kWarp>
-__device__ __forceinline__ unsigned int warp_bcast(unsigned int v) {
-    if constexpr (kWarp) return __shfl_sync(0xffffffffu, v, 0);
-    return v;
-}
-
 // ---------------------------------------------------------------------------
-// Producer: streams every tile of the chunks this CTA claims into the ring.
-// One lane, or (fused append) the whole warp, with lane 0 issuing the copies.
+// Producer: one lane streams every tile of the chunks this CTA claims into
+// the ring.
 template <int D, int BS, bool kHalfKV, int APPEND>
 __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* smem,
                                                 uint64_t* full, uint64_t* empty,
                                                 TileMeta* meta, CtaCtl* ctl) {
     using C = DecodeCfg<D, BS, kHalfKV>;
-    constexpr bool kWarp = APPEND != kNoAppend;
-    static_assert(!(kWarp && kHalfKV), "fused append is INT8 only");
-    const bool leader = !kWarp || (threadIdx.x & 31) == 0;
+    constexpr bool kAppend = APPEND != kNoAppend;
+    static_assert(!(kAppend && kHalfKV), "fused append is INT8 only");
     const uint64_t policy = make_evict_first_policy();
     const uint64_t q_lo = reinterpret_cast<uint64_t>(a.q);
     const uint64_t q_hi = q_lo + static_cast<uint64_t>(a.BH) * D * 2;
@@ -339,7 +336,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     const uint64_t sc_bytes = static_cast<uint64_t>(a.BH) * a.S_stride * C::kNSub * 2;
     const uint8_t* kbase = static_cast<const uint8_t*>(a.k);
     const uint8_t* vbase = static_cast<const uint8_t*>(a.v);
-    const int first_new = kWarp ? a.S - a.T_new : a.S;  // rows >= first_new are appended
+    const int first_new = kAppend ? a.S - a.T_new : a.S;  // rows >= first_new are appended
 
     int stage = 0;
     uint32_t phase = 0;
@@ -350,10 +347,9 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     // of a split head (and their indices) deterministic.
     unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
     while (ok) {
-        unsigned int chunk = 0;
+        unsigned int chunk;
         if (a.sched != nullptr) {
-            if (leader) chunk = atomicAdd(&a.sched[0], 1u);
-            chunk = warp_bcast<kWarp>(chunk);
+            chunk = atomicAdd(&a.sched[0], 1u);
         } else {
             chunk = static_chunk;
             static_chunk += gridDim.x;
@@ -370,17 +366,13 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             const long long u_last = (head0 + a.S - 1) / a.chunk_rows;
             for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
                 const int cnt = (t_b - t0) < C::kTile ? (t_b - t0) : C::kTile;
-                unsigned int got = 0;  // 0: stage free, 1: aborted, 2: wait gave up
-                if (leader) {
-                    if (ld_volatile_shared(&ctl->abort)) {
-                        got = 1;
-                    } else if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
-                        record_device_error(kErrEmptyWaitTimeout);
-                        atomicExch(&ctl->abort, 1u);
-                        got = 2;
-                    }
+                if (ld_volatile_shared(&ctl->abort)) {
+                    ok = false;
+                    break;
                 }
-                if (warp_bcast<kWarp>(got) != 0u) {
+                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+                    record_device_error(kErrEmptyWaitTimeout);
+                    atomicExch(&ctl->abort, 1u);
                     ok = false;
                     break;
                 }
@@ -391,18 +383,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
                 nb = nb < 0 ? 0 : (nb > cnt ? cnt : nb);
                 const uint64_t ks_src = ks_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
                 const uint64_t vs_src = vs_lo + static_cast<uint64_t>(row0) * C::kNSub * 2;
-                if constexpr (kWarp) {
-                    // nb is warp-uniform; a tile without new rows needs no
-                    // warp barrier (and no fence that could wait on earlier
-                    // memory operations of the leader)
-                    if (nb < cnt) {
-                        append_rows<D, BS, APPEND>(a, st, bh, t0, nb, cnt, row0,
-                                                   static_cast<int>(ks_src & 15),
-                                                   static_cast<int>(vs_src & 15));
-                        __syncwarp();  // orders the lanes' shared stores before the arrive
-                    }
-                }
-                if (leader) {
+                {
                     const uint32_t kv_bytes = static_cast<uint32_t>(nb) * C::kRowBytes;
                     uint32_t tx = 2 * kv_bytes;
 
@@ -413,13 +394,14 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
                     m.flags = (t0 == t_a ? kTileFirst : 0) | (t0 + C::kTile >= t_b ? kTileLast : 0);
                     m.part = static_cast<int>(chunk - u_first);
                     m.nparts = static_cast<int>(u_last - u_first + 1);
+                    m.n_old = nb;
 
                     Span sk{}, sv{}, sq{};
                     uint64_t q_src = 0;
                     if constexpr (!kHalfKV) {
                         const uint32_t sc_n = static_cast<uint32_t>(nb) * C::kNSub * 2;
                         // with appended rows the bulk span must stop short of their
-                        // scales, which the warp has written into the same slot
+                        // scales, which the consumers write into the same slot
                         const uint64_t k_hi = nb < cnt ? ks_src + sc_n : ks_lo + sc_bytes;
                         const uint64_t v_hi = nb < cnt ? vs_src + sc_n : vs_lo + sc_bytes;
                         sk = plan_span(ks_src, sc_n, ks_lo, k_hi);
@@ -467,7 +449,6 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             r = head0 + t_b;
         }
     }
-    if (!leader) return;
     // end-of-work marker for the consumers
     if (ok) {
         if (mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
@@ -1007,7 +988,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
 
     const int warp = threadIdx.x >> 5;
     if (warp == kDecodeConsumerWarps) {
-        if (APPEND != kNoAppend || (threadIdx.x & 31) == 0)
+        if ((threadIdx.x & 31) == 0)
             decode_producer<D, BS, kHalfKV, APPEND>(a, smem, full, empty, meta, ctl);
         return;
     }
@@ -1043,6 +1024,14 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
             const long long mrow0 = static_cast<long long>(m.bh) * a.S_stride + m.t0;
             ks_off = scale_slot_offset(a.ks, mrow0, C::kNSub);
             vs_off = scale_slot_offset(a.vs, mrow0, C::kNSub);
+            if constexpr (APPEND != kNoAppend) {
+                if (m.n_old < m.cnt) {  // CTA-uniform: new rows in this tile
+                    append_rows<D, BS, APPEND>(a, const_cast<uint8_t*>(sp), m.bh, m.t0,
+                                               m.n_old + warp, m.cnt, kDecodeConsumerWarps,
+                                               mrow0, ks_off, vs_off);
+                    if (!consumer_barrier(ctl)) return;
+                }
+            }
         }
         consume_tile<D, BS, kHalfKV>(st, sp, m.cnt, ks_off, vs_off, g, r);
         __syncwarp();

@@ -63,8 +63,8 @@ def plan_span(src, n, lo, hi):
 
 
 def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
-    """T_new > 0: the fused-append variant, whose tiles take rows >= S - T_new
-    from the producer warp instead of the bulk copies."""
+    """T_new > 0: the fused-append variant, whose tiles get rows >= S - T_new
+    from the consumer warps' quantisation instead of the bulk copies."""
     S_stride = S if S_stride is None else S_stride
     elem = 2 if half else 1
     RB = D * elem
@@ -116,7 +116,7 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
                     b_src, b_off, b_n = plan_span(src, n, sbase, hi)
                     if nb < cnt:
                         # the bulk copy stops short of the new rows' scales,
-                        # which the producer warp writes into the same slot
+                        # which the consumer warps write into the same slot
                         assert not b_n or b_off + b_n <= (src & 15) + n
                         for t in range(nb, cnt):
                             for j in range(nsub):
