@@ -36,7 +36,6 @@ import math
 import os
 import statistics
 import sys
-import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -102,9 +101,34 @@ def traffic_per_launch(workload_name: str, n_gpus: int):
 
 
 # ---------------------------------------------------------------------------
+# NVML sampling loop, run in a child process so that it keeps sampling while
+# the benchmark's main thread sits in CUDA calls (which can hold the GIL when
+# the launch queue is full).  Prints "ready", then one line per sample:
+# "sm_mhz mem_mhz power_mw reasons_mask", until its stdin closes.
+_SAMPLER_SRC = r"""
+import sys, threading, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+interval = float(sys.argv[2])
+stop = threading.Event()
+threading.Thread(target=lambda: (sys.stdin.read(), stop.set()), daemon=True).start()
+print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while not stop.is_set():
+    try:
+        print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+              pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_MEM),
+              pynvml.nvmlDeviceGetPowerUsage(h),
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    except pynvml.NVMLError:
+        pass
+    time.sleep(interval)
+"""
+
+
 class ClockSampler:
-    """Samples SM clock and clock-event (throttle) reasons with NVML in a
-    background thread while the timed region runs."""
+    """Samples SM clock, memory clock, power and clock-event (throttle)
+    reasons with NVML from a child process while the timed region runs."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -117,43 +141,41 @@ class ClockSampler:
         self.samples, self.reasons = [], set()
         self.mem_mhz, self.power_w = [], []
         self.max_mhz = None
-        self.interval = interval_s
-        self._stop = threading.Event()
-        self._thread = None
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-        except Exception:
-            self.nv = None
-
-    def _run(self):
-        nv = self.nv
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                self.mem_mhz.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_MEM))
-                self.power_w.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if mask & bit and name != "gpu_idle":
-                        self.reasons.add(name)
-            except Exception:
-                pass
-            time.sleep(self.interval)
+        self.device_index, self.interval = device_index, interval_s
+        self.proc = None
 
     def __enter__(self):
-        if self.nv is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+        import subprocess
+        try:
+            self.proc = subprocess.Popen(
+                [sys.executable, "-c", _SAMPLER_SRC, str(self.device_index), str(self.interval)],
+                stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            first = self.proc.stdout.readline().split()
+            if first[:1] == ["ready"]:
+                self.max_mhz = int(first[1])
+            else:
+                self.proc.kill()
+                self.proc = None
+        except Exception:
+            self.proc = None
         return self
 
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join()
+        if self.proc is None:
+            return
+        out, _ = self.proc.communicate(input="", timeout=30)
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) != 4:
+                continue
+            sm, mem, mw, mask = (int(x) for x in f)
+            self.samples.append(sm)
+            self.mem_mhz.append(mem)
+            self.power_w.append(mw / 1000.0)
+            for bit, name in self.REASONS.items():
+                if mask & bit and name != "gpu_idle":
+                    self.reasons.add(name)
 
     def summary(self):
         if not self.samples:
@@ -586,7 +608,8 @@ def main():
                 "step": "H2D q, k_new, v_new (pinned) -> " +
                         ("append k, v to the int8 cache (separate launches) -> decode"
                          if collective and not use_p2p else
-                         "decode with the append of k, v fused in (tqkv_decode_int8_append)") +
+                         "decode with the append of k, v fused in (tqkv_decode_int8_append" +
+                         ("_publish on the rank holding the newest tokens)" if collective else ")")) +
                         (" -> exchange + combine" if collective else "") + " -> D2H O -> host sync"},
         "gpu_launches": args.steps * (2 if collective else 1),
         "clocks": clk.summary(),

@@ -106,10 +106,10 @@ struct DecodeArgs {
     const uint16_t* ks;        // fp16 [BH][S][D/BS] (INT8 only)
     const uint16_t* vs;
     void* out;                 // fp16 O [BH][D] or float [BH][D+2]
-    float* parts;              // workspace [BH][max_parts][D+2] (log2 units)
+    float* parts;              // workspace [BH][max_parts][D+4] (log2 units; see kRecFloats)
     unsigned int* tickets;     // workspace [BH]
     long long total_rows;      // BH * S
-    long long chunk_rows;      // rows per scheduling chunk (C)
+    long long chunk_rows;      // C: chunk u is rows [u * C, (u + 1) * C) of the BH * S rows
     unsigned int nchunks;      // ceil(total_rows / C)
     unsigned int* sched;       // workspace: [0] next chunk to hand out, [1] producers done
     int S;                     // rows attended per head
@@ -145,9 +145,21 @@ struct DecodeCfg {
     static constexpr int kStageBytes = kOffQ + kQSlot;
     // merge scratch after the ring
     static constexpr int kOffMerge = kDecodeStages * kStageBytes;
-    static constexpr int kMergeBytes = kDecodeConsumerWarps * (D + 2) * 4;
-    // the split-head merge reuses it for one weight per consumer thread + 8 sums
-    static_assert(kMergeBytes >= (kDecodeConsumers + 2 * kDecodeConsumerWarps) * 4, "merge area");
+    // Workspace record of a split head's piece: acc[D], m, l, 2 floats of
+    // padding, so that records start on 16 bytes and merge with float4 loads.
+    static constexpr int kRecFloats = D + 4;
+    // The merge of a split head splits the D dims into float4 groups over
+    // kRecLanes threads and the records into kRecSlices slices.
+    static constexpr int kRecLanes = D / 4;
+    static constexpr int kRecSlices = kDecodeConsumers / kRecLanes;
+    // merge area: the warps' states; or, merging records, one weight per
+    // consumer thread / the slices' partial sums, then 8 reduction slots
+    static constexpr int kMergeFloats =
+        kDecodeConsumerWarps * (D + 2) > kRecSlices * D + 2 * kDecodeConsumerWarps
+            ? kDecodeConsumerWarps * (D + 2)
+            : kRecSlices * D + 2 * kDecodeConsumerWarps;
+    static constexpr int kMergeBytes = kMergeFloats * 4;
+    static_assert(kRecSlices * D >= kDecodeConsumers, "weights fit under the slice sums");
     static constexpr int kOffBars = kOffMerge + kMergeBytes;
     static constexpr int kOffMeta = kOffBars + 2 * kDecodeStages * 8;  // int[stages][8]
     static constexpr int kOffCtl = kOffMeta + kDecodeStages * 32;      // CtaCtl
@@ -167,54 +179,41 @@ struct TileMeta {
     int pad;
 };
 
-// CTA control block in shared memory: the consumer warps' software barrier
-// (bounded, see consumer_barrier), the merge flag, and an abort flag that any
-// warp whose bounded wait ran out raises so that the others leave as well.
+// CTA control block in shared memory: the merge flag, and an abort flag that
+// a warp whose bounded wait ran out raises so that the others leave as well.
 struct CtaCtl {
     int flag;
-    unsigned int bar_count;
-    unsigned int bar_gen;
     unsigned int abort;
-    unsigned int pad[4];
+    unsigned int pad[6];
 };
+static_assert(sizeof(CtaCtl) == 32, "CtaCtl layout");
+
+constexpr int kConsumerBarrier = 1;  // named barrier of the consumer warps (id 0: __syncthreads)
 
 __device__ __forceinline__ unsigned int ld_volatile_shared(const unsigned int* p) {
     return *reinterpret_cast<const volatile unsigned int*>(p);
 }
 
-// Barrier of the consumer warps.  Unlike bar.sync it cannot hang: a warp that
-// waits longer than ~2^31 cycles, or sees the abort flag, returns false (and
-// raises abort), and the caller leaves the kernel.
+// Barrier of the consumer warps (bar.sync on kConsumerBarrier).  Returns
+// false when the CTA is aborting; the caller then leaves through
+// consumer_leave.
+//
+// Why it cannot hang: a consumer warp only ever leaves the kernel early
+// through consumer_leave, which raises the abort flag and then arrives once
+// at the consumer barrier.  The consumer warps pass the same sequence of
+// barrier instances, so a leaving warp's arrival stands in for it at the
+// instance the others are waiting at (or will reach next); that instance
+// completes, and every warp sees the abort flag right after it and leaves.
 __device__ __forceinline__ bool consumer_barrier(CtaCtl* c) {
+    named_barrier_sync(kConsumerBarrier, kDecodeConsumers);
+    return ld_volatile_shared(&c->abort) == 0u;
+}
+
+__device__ __forceinline__ void consumer_leave(CtaCtl* c) {
+    if ((threadIdx.x & 31) == 0) atomicExch(&c->abort, 1u);
     __threadfence_block();
     __syncwarp();
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) {
-        const unsigned int gen = ld_volatile_shared(&c->bar_gen);
-        if (atomicAdd(&c->bar_count, 1u) == static_cast<unsigned int>(kDecodeConsumerWarps - 1)) {
-            c->bar_count = 0u;
-            __threadfence_block();
-            atomicAdd(&c->bar_gen, 1u);
-        } else {
-            const long long start = clock64();
-            while (ld_volatile_shared(&c->bar_gen) == gen) {
-                if (ld_volatile_shared(&c->abort)) {
-                    ok = 0;
-                    break;
-                }
-                if (clock64() - start > (1ll << 31)) {
-                    record_device_error(kErrBarrierTimeout);
-                    atomicExch(&c->abort, 1u);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        __threadfence_block();
-    }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    __syncwarp();
-    return ok != 0;
+    named_barrier_arrive(kConsumerBarrier, kDecodeConsumers);
 }
 
 // Bytes [src, src + n) (src even, n even) of the buffer [lo, hi) land in
@@ -342,9 +341,11 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     uint32_t phase = 0;
     long long issued = 0;
     bool ok = true;
-    // Chunks of C rows are handed out dynamically, so SMs that stream faster
-    // take more of them; chunk boundaries are fixed, which keeps the pieces
-    // of a split head (and their indices) deterministic.
+    // Chunks are taken statically (chunk = blockIdx.x) or, with a scheduler,
+    // handed out dynamically so that SMs that stream faster take more of them.
+    // Chunk boundaries are fixed either way, which keeps the pieces of a split
+    // head (and their indices) deterministic.  A chunk may cover the end of
+    // one head and the start of the next: one segment per head.
     unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
     while (ok) {
         unsigned int chunk;
@@ -362,6 +363,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             const long long head0 = static_cast<long long>(bh) * a.S;
             const int t_a = static_cast<int>(r - head0);
             const int t_b = static_cast<int>((c1 - head0) < a.S ? (c1 - head0) : a.S);
+            // the chunks holding pieces of this head: u_first .. u_last
             const long long u_first = head0 / a.chunk_rows;
             const long long u_last = (head0 + a.S - 1) / a.chunk_rows;
             for (int t0 = t_a; t0 < t_b; t0 += C::kTile) {
@@ -889,7 +891,7 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
     }
 
     // publish this CTA's piece of the head
-    float* mine = a.parts + (static_cast<long long>(bh) * a.max_parts + part) * (D + 2);
+    float* mine = a.parts + (static_cast<long long>(bh) * a.max_parts + part) * C::kRecFloats;
     if (tid < D) {
         mine[tid] = A;
         if (tid == 0) {
@@ -897,24 +899,31 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
             mine[D + 1] = L;
         }
     }
-    __threadfence();
+    // every thread's record stores happen before thread 0's fence through the
+    // barrier, and the fence (cumulative) orders them before the ticket
     if (!consumer_barrier(ctl)) return false;
     if (tid == 0) {
+        __threadfence();
         const unsigned int prev = atomicAdd(&a.tickets[bh], 1u);
         ctl->flag = (prev == static_cast<unsigned int>(nparts - 1)) ? 1 : 0;
     }
     if (!consumer_barrier(ctl)) return false;
-    if (*reinterpret_cast<volatile int*>(&ctl->flag)) {
+    // Not the last piece: done.  Every read of merge[] happened before the
+    // barrier after the record stores, so the next segment may overwrite it.
+    if (!*reinterpret_cast<volatile int*>(&ctl->flag)) return true;
+    {
         // Last piece of the head: merge its nparts records.  The records are
         // spread over the consumer threads (one per thread for the maxima and
-        // weights) so the L2 reads overlap instead of running one by one.
+        // weights; float4 groups of dims x record slices for acc) so the L2
+        // reads overlap instead of running one by one.
         __threadfence();
-        const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
-        float* fw = merge;                          // weights of one batch of records
-        float* red = merge + kDecodeConsumers;      // [0..3] warp maxima, [4..7] warp sums
+        constexpr int kRec = C::kRecFloats;
+        const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * kRec;
+        float* fw = merge;                                  // weights of one batch of records
+        float* red = merge + C::kRecSlices * D;             // [0..3] warp maxima, [4..7] sums
         float mloc = -INFINITY;
         for (int p = tid; p < nparts; p += kDecodeConsumers)
-            mloc = fmaxf(mloc, __ldcg(recs + p * (D + 2) + D));
+            mloc = fmaxf(mloc, __ldcg(recs + p * kRec + D));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1)
             mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
@@ -924,36 +933,50 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
 #pragma unroll
         for (int w = 1; w < kDecodeConsumerWarps; ++w) Mt = fmaxf(Mt, red[w]);
         const float base = Mt == -INFINITY ? 0.0f : Mt;
-        float At = 0.0f, Lloc = 0.0f;
+        const int dq = tid % C::kRecLanes;   // dims 4*dq .. 4*dq + 3
+        const int sl = tid / C::kRecLanes;   // records sl, sl + kRecSlices, ...
+        float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float Lloc = 0.0f;
         for (int b0 = 0; b0 < nparts; b0 += kDecodeConsumers) {
             const int nb = (nparts - b0) < kDecodeConsumers ? (nparts - b0) : kDecodeConsumers;
             if (tid < nb) {
-                const float* rp = recs + (b0 + tid) * (D + 2);
+                const float* rp = recs + (b0 + tid) * kRec;
                 const float f = fast_exp2(__ldcg(rp + D) - base);
                 fw[tid] = f;
                 Lloc = fmaf(__ldcg(rp + D + 1), f, Lloc);
             }
             if (!consumer_barrier(ctl)) return false;
-            if (tid < D) {
-                const float* rp = recs + b0 * (D + 2) + tid;
-#pragma unroll 8
-                for (int k = 0; k < nb; ++k) At = fmaf(__ldcg(rp + k * (D + 2)), fw[k], At);
+            const float4* rp = reinterpret_cast<const float4*>(recs + b0 * kRec) + dq;
+#pragma unroll 4
+            for (int k = sl; k < nb; k += C::kRecSlices) {
+                const float4 r = __ldcg(rp + k * (kRec / 4));
+                const float f = fw[k];
+                acc4.x = fmaf(r.x, f, acc4.x);
+                acc4.y = fmaf(r.y, f, acc4.y);
+                acc4.z = fmaf(r.z, f, acc4.z);
+                acc4.w = fmaf(r.w, f, acc4.w);
             }
             if (b0 + kDecodeConsumers < nparts && !consumer_barrier(ctl)) return false;
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) Lloc += __shfl_xor_sync(0xffffffffu, Lloc, off);
         if (lane == 0) red[kDecodeConsumerWarps + warp] = Lloc;
-        // every record has been read once all warps pass this barrier
+        // every record (and weight) has been read once all warps pass this barrier
         if (!consumer_barrier(ctl)) return false;
-        float Lt = 0.0f;
+        *reinterpret_cast<float4*>(merge + sl * D + 4 * dq) = acc4;
+        if (!consumer_barrier(ctl)) return false;
+        float At = 0.0f, Lt = 0.0f;
+        if (tid < D) {
+#pragma unroll
+            for (int k = 0; k < C::kRecSlices; ++k) At += merge[k * D + tid];
+        }
 #pragma unroll
         for (int w = 0; w < kDecodeConsumerWarps; ++w) Lt += red[kDecodeConsumerWarps + w];
         emit_head<D, OUT>(a, bh, tid, At, Mt, Lt);
         // leave the workspace all-zero for the next call, whatever its shape:
         // the ticket, and every record this merge consumed
-        float* zrec = a.parts + static_cast<long long>(bh) * a.max_parts * (D + 2);
-        for (int i = tid; i < nparts * (D + 2); i += kDecodeConsumers) zrec[i] = 0.0f;
+        float* zrec = a.parts + static_cast<long long>(bh) * a.max_parts * kRec;
+        for (int i = tid; i < nparts * kRec; i += kDecodeConsumers) zrec[i] = 0.0f;
         if (tid == 0) a.tickets[bh] = 0u;
     }
     return consumer_barrier(ctl);
@@ -979,8 +1002,6 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
             mbar_init(&empty[i], kDecodeConsumerWarps);
         }
         ctl->flag = 0;
-        ctl->bar_count = 0u;
-        ctl->bar_gen = 0u;
         ctl->abort = 0u;
         fence_barrier_init();
     }
@@ -1005,10 +1026,8 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         const bool ok = mbar_wait_bounded(&full[stage], phase);
         // warp-uniform decision: every lane leaves, or none does
         if (__any_sync(0xffffffffu, !ok || ld_volatile_shared(&ctl->abort) != 0u)) {
-            if (lane == 0) {
-                if (!ok) record_device_error(kErrFullWaitTimeout);
-                atomicExch(&ctl->abort, 1u);
-            }
+            if (lane == 0 && !ok) record_device_error(kErrFullWaitTimeout);
+            consumer_leave(ctl);
             return;
         }
         const TileMeta m = meta[stage];
@@ -1029,7 +1048,10 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                     append_rows<D, BS, APPEND>(a, const_cast<uint8_t*>(sp), m.bh, m.t0,
                                                m.n_old + warp, m.cnt, kDecodeConsumerWarps,
                                                mrow0, ks_off, vs_off);
-                    if (!consumer_barrier(ctl)) return;
+                    if (!consumer_barrier(ctl)) {
+                        consumer_leave(ctl);
+                        return;
+                    }
                 }
             }
         }
@@ -1041,8 +1063,11 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
             phase ^= 1u;
         }
         if (m.flags & kTileLast) {
-            if (!finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, ctl, m.bh, m.part, m.nparts, tid))
+            if (!finish_segment<D, BS, kHalfKV, OUT>(st, a, merge, ctl, m.bh, m.part, m.nparts,
+                                                     tid)) {
+                consumer_leave(ctl);
                 return;
+            }
         }
     }
 }

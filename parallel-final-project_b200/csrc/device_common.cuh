@@ -21,7 +21,6 @@ enum DeviceErrorCode : unsigned int {
     kErrEmptyWaitTimeout = 2,    // producer waited too long for a free stage
     kErrDrainTimeout = 3,        // producer's copies never completed
     kErrPeerWaitTimeout = 4,     // a peer GPU's exchange entries never arrived
-    kErrBarrierTimeout = 5,      // a consumer warp never reached a CTA barrier
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {
@@ -132,6 +131,11 @@ __device__ __forceinline__ bool wait_flag_bounded(const unsigned int* flag, unsi
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Arrive at a named barrier without waiting for it.
+__device__ __forceinline__ void named_barrier_arrive(int id, int nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // 2^x, hardware approximation (MUFU.EX2), flush-to-zero; ex2(-inf) = +0.

@@ -43,9 +43,11 @@ constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipelin
 constexpr long long kChunksPerCta = 8;     // scheduling chunks per CTA (load balance)
 constexpr long long kChunkAlign = 128;     // chunk rows: a multiple of every tile height
 // Below this many rows per CTA every CTA takes one run of rows, statically:
-// the runs are short, so a chunk claim and a split-head merge per chunk
-// would cost more than the imbalance they remove.
-constexpr long long kMinDynamicRowsPerCta = 2048;
+// each chunk boundary costs a head piece (a record, a ticket and consumer
+// barriers), which short chunks cannot amortise.  Measured on one B200 with
+// 592 CTAs: dynamic chunks win 1.4 % at 28k rows per CTA (long-context
+// decode), and lose 14 % at 7k rows per CTA (B16 H32 S8192).
+constexpr long long kMinDynamicRowsPerCta = 16384;
 constexpr int kMaxCtasPerSmBound = 4;      // >= any decode kernel's occupancy (smem-bound)
 
 struct KernelKey {
@@ -98,14 +100,17 @@ struct DecodePlan {
     int max_parts;
 };
 
-// Rows are cut into fixed chunks of C rows.  With many rows per CTA there are
-// about kChunksPerCta chunks per CTA, claimed dynamically, so SMs that stream
-// faster take more of them; otherwise one chunk per CTA (a static run, C
-// rounded to 16 rows).  `max_ctas` caps the grid (resident CTAs).  C does not
-// grow with max_ctas, so a bound plan computed with the largest grid has the
-// most parts per head.
-DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
+// The B*H*S rows, heads laid end to end, are cut into fixed chunks of C rows.
+// Normally there is one chunk per CTA (C = rows / grid, rounded to 16): equal
+// work for every CTA and the fewest head pieces.  When a CTA would stream at
+// least kMinDynamicRowsPerCta rows, C is cut to about 1/kChunksPerCta of that
+// (a multiple of 128) and the CTAs claim chunks dynamically, so SMs that
+// stream faster take more of them; each chunk is then long enough (>= 32
+// tiles) to amortise the extra head pieces it creates.  `max_ctas` caps the
+// grid (resident CTAs).
+DecodePlan make_plan(long long BH, int S, long long max_ctas) {
     DecodePlan p{};
+    const long long total_rows = BH * S;
     long long g = (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta;
     if (g > max_ctas) g = max_ctas;
     if (g < 1) g = 1;
@@ -126,11 +131,11 @@ DecodePlan make_plan(long long total_rows, int S, long long max_ctas) {
 // The workspace layout is fixed by an upper bound on the parts per head over
 // every grid cap a decode kernel can have (SMs x 1..kMaxCtasPerSmBound
 // resident CTAs), so that its size does not depend on which kernel runs.
-DecodePlan bound_plan(long long total_rows, int S, int device) {
+DecodePlan bound_plan(long long BH, int S, int device) {
     const long long sms = sm_count(device) > 0 ? sm_count(device) : 1;
-    DecodePlan b = make_plan(total_rows, S, sms);
+    DecodePlan b = make_plan(BH, S, sms);
     for (long long occ = 2; occ <= kMaxCtasPerSmBound; ++occ) {
-        const DecodePlan p = make_plan(total_rows, S, sms * occ);
+        const DecodePlan p = make_plan(BH, S, sms * occ);
         if (p.max_parts > b.max_parts) b = p;
     }
     return b;
@@ -150,7 +155,7 @@ WsLayout ws_layout(long long BH, int max_parts, int D) {
     w.tickets_off = 16;
     w.parts_off = decode_ws_counter_bytes(BH);
     w.total = w.parts_off +
-              align_up(static_cast<size_t>(BH) * max_parts * (D + 2) * sizeof(float), 256);
+              align_up(static_cast<size_t>(BH) * max_parts * (D + 4) * sizeof(float), 256);
     return w;
 }
 
@@ -224,11 +229,12 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     const int per_sm = prepare_kernel(fn, kDecodeThreads, C::kSmemBytes, dev);
     if (per_sm <= 0) return from_cuda(cudaErrorInvalidConfiguration);
 
-    const DecodePlan bound = bound_plan(total_rows, S, dev);
+    const DecodePlan bound = bound_plan(BH, S, dev);
     const WsLayout lay = ws_layout(BH, bound.max_parts, D);
     const long long resident = static_cast<long long>(sm_count(dev)) * per_sm;
-    const DecodePlan plan = make_plan(total_rows, S, resident);
+    const DecodePlan plan = make_plan(BH, S, resident);
     if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: per_sm <= bound
+    // records and tickets for cut heads; the claim counter for dynamic chunks
     const bool needs_ws = plan.nchunks > 1;
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
 
@@ -238,7 +244,7 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
                                         : nullptr;
     a.tickets = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.tickets_off) : nullptr;
     a.parts = needs_ws ? reinterpret_cast<float*>(ws + lay.parts_off) : nullptr;
-    a.total_rows = total_rows;
+    a.total_rows = static_cast<long long>(BH) * S;
     a.chunk_rows = plan.chunk_rows;
     a.nchunks = static_cast<unsigned int>(plan.nchunks);
     a.S = S;
@@ -425,7 +431,7 @@ size_t decode_workspace_bytes(long long BH, int S, int D) {
     if (BH <= 0 || S <= 0) return 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    const DecodePlan bound = bound_plan(BH * S, S, dev);
+    const DecodePlan bound = bound_plan(BH, S, dev);
     return ws_layout(BH, bound.max_parts, D).total;
 }
 

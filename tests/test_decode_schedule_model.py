@@ -42,8 +42,9 @@ BOUND_OCC = _const("tqkv_capi.cu", "kMaxCtasPerSmBound")
 SMS = 148
 
 
-def make_plan(total, S, max_ctas):
+def make_plan(BH, S, max_ctas):
     """(grid, chunk rows C, number of chunks, max_parts)"""
+    total = BH * S
     g = max(min(-(-total // MIN_ROWS), max_ctas), 1)
     c = -(-total // g)
     if c >= MIN_DYNAMIC:
@@ -76,11 +77,11 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
     slot = 0 if half else TILE * nsub * 2 + 32
     qslot = D * 2 + 32
     total = BH * S
-    grid, R, nchunks, _ = make_plan(total, S, SMS * occ)
+    grid, R, nchunks, _ = make_plan(BH, S, SMS * occ)
     # workspace layout bound: the most parts per head over every grid cap
-    maxp = max(make_plan(total, S, SMS * o)[3] for o in range(1, BOUND_OCC + 1))
+    maxp = max(make_plan(BH, S, SMS * o)[3] for o in range(1, BOUND_OCC + 1))
     assert 1 <= grid <= nchunks and nchunks < 2 ** 32
-    if nchunks == 1:      # no workspace: every head must be one piece
+    if nchunks == 1:      # no workspace: the one chunk holds every head whole
         assert R >= total
     kbase, sbase, qbase = 1 << 40, (1 << 41) + offs[0], (1 << 42) + offs[1]
     k_end = kbase + BH * S_stride * RB
