@@ -156,6 +156,22 @@ tqkv_status tqkv_decode_int8_append(const void* q, const void* k_new, const void
                                     void* workspace, size_t workspace_bytes,
                                     cudaStream_t stream);
 
+/* Grouped-query / multi-query attention (no counterpart in the reference,
+ * whose K/V have one head per query head).  q and o are [B, H_q, D]; kq/vq
+ * int8 [B, H_kv, S, D] and ks/vs fp16 [B, H_kv, S, D / block_size], with
+ * H_q a multiple of H_kv: query head h attends over K/V head h / (H_q / H_kv)
+ * (MQA: H_kv = 1).  The result equals tqkv_decode_int8 on K/V whose heads
+ * are repeated H_q / H_kv times.  Query heads that share a K/V head run on
+ * neighbouring CTAs, so their K/V reads meet in L2.  Workspace:
+ * tqkv_decode_workspace_bytes(B, H_q, S, D). */
+tqkv_status tqkv_decode_int8_gqa(const void* q,
+                                 const int8_t* kq, const void* ks,
+                                 const int8_t* vq, const void* vs,
+                                 void* o,
+                                 int B, int H_q, int H_kv, int S, int D, int block_size,
+                                 void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
+
 /* FP16 decode attention on the same split-S skeleton.
  * Replaces launch_decode_attn_baseline (reference include/attention.h:6-12,
  * src/attention_baseline.cu:11-155) without its S <= ~12k shared-memory cap.

@@ -114,6 +114,7 @@ struct DecodeArgs {
     unsigned int* sched;       // workspace: [0] next chunk to hand out, [1] producers done
     int S;                     // rows attended per head
     int S_stride;              // rows between consecutive heads in K/V/scales (>= S)
+    int group;                 // query heads per K/V head (GQA/MQA; 1 = one K/V head each)
     int BH;
     int max_parts;
     float score_scale_log2;    // log2(e) / sqrt(D)
@@ -332,7 +333,8 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     const uint64_t q_hi = q_lo + static_cast<uint64_t>(a.BH) * D * 2;
     const uint64_t ks_lo = reinterpret_cast<uint64_t>(a.ks);
     const uint64_t vs_lo = reinterpret_cast<uint64_t>(a.vs);
-    const uint64_t sc_bytes = static_cast<uint64_t>(a.BH) * a.S_stride * C::kNSub * 2;
+    const uint64_t sc_bytes =
+        static_cast<uint64_t>(a.BH / a.group) * a.S_stride * C::kNSub * 2;
     const uint8_t* kbase = static_cast<const uint8_t*>(a.k);
     const uint8_t* vbase = static_cast<const uint8_t*>(a.v);
     const int first_new = kAppend ? a.S - a.T_new : a.S;  // rows >= first_new are appended
@@ -379,7 +381,8 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
                     break;
                 }
                 uint8_t* st = smem + stage * C::kStageBytes;
-                const long long row0 = static_cast<long long>(bh) * a.S_stride + t0;  // memory row
+                // memory row: K/V head bh / group holds this query head's keys
+                const long long row0 = static_cast<long long>(bh / a.group) * a.S_stride + t0;
                 // rows [0, nb) of the tile come from the cache, [nb, cnt) are new
                 int nb = first_new - t0;
                 nb = nb < 0 ? 0 : (nb > cnt ? cnt : nb);
@@ -1040,7 +1043,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         }
         int ks_off = 0, vs_off = 0;
         if constexpr (!kHalfKV) {
-            const long long mrow0 = static_cast<long long>(m.bh) * a.S_stride + m.t0;
+            const long long mrow0 = static_cast<long long>(m.bh / a.group) * a.S_stride + m.t0;
             ks_off = scale_slot_offset(a.ks, mrow0, C::kNSub);
             vs_off = scale_slot_offset(a.vs, mrow0, C::kNSub);
             if constexpr (APPEND != kNoAppend) {

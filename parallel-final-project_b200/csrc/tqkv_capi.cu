@@ -220,8 +220,10 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
 template <int D, int BS, bool kHalfKV, int OUT, int APPEND = kNoAppend>
 tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void* workspace,
                         size_t workspace_bytes, cudaStream_t stream) {
-    // a.peer is set by the caller (kOutPeers) or zero; a.S_stride by the caller
+    // a.peer is set by the caller (kOutPeers) or zero; a.S_stride and a.group
+    // by the caller
     using C = DecodeCfg<D, BS, kHalfKV>;
+    if (a.group < 1 || BH % a.group != 0) return TQKV_ERR_INVALID_SIZE;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return from_cuda(e);
@@ -290,6 +292,7 @@ tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void*
     a.out = nullptr;
     a.peer = peer;
     a.S_stride = S_stride > 0 ? S_stride : S;
+    a.group = 1;
     if (append != nullptr) {
         a.k_new = append->k_new;
         a.v_new = append->v_new;
@@ -377,9 +380,11 @@ tqkv_status launch_reconstruct(const int8_t* xq, const void* scales, void* y, lo
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D, int bs,
                           void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                          int S_stride, const AppendRows* append) {
+                          int S_stride, const AppendRows* append, int group) {
     DecodeArgs a{};
     a.S_stride = S_stride > 0 ? S_stride : S;
+    a.group = group;
+    if (group > 1 && append != nullptr) return TQKV_ERR_UNSUPPORTED;
     if (append != nullptr) {
         if (kv != KvKind::kInt8) return TQKV_ERR_UNSUPPORTED;
         a.k_new = append->k_new;
@@ -576,6 +581,23 @@ tqkv_status tqkv_decode_int8_append(const void* q, const void* k_new, const void
     return tqkv::launch_decode(KvKind::kInt8, OutKind::kHalfO, q, kq, ks, vq, vs, o,
                                static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
                                stream, S_cap, &rows);
+}
+
+tqkv_status tqkv_decode_int8_gqa(const void* q, const int8_t* kq, const void* ks,
+                                 const int8_t* vq, const void* vs, void* o, int B, int H_q,
+                                 int H_kv, int S, int D, int block_size, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream) {
+    if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
+    if (B <= 0 || H_q <= 0 || H_kv <= 0 || S < 0 || H_q % H_kv != 0) return TQKV_ERR_INVALID_SIZE;
+    if (!q || !o) return TQKV_ERR_NULL;
+    const long long BH = static_cast<long long>(B) * H_q;
+    if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
+    if (S == 0) return tqkv::launch_fill_half(o, BH * D, 0x7e00u, stream);
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode(KvKind::kInt8, OutKind::kHalfO, q, kq, ks, vq, vs, o,
+                               static_cast<int>(BH), S, D, block_size, workspace, workspace_bytes,
+                               stream, S, nullptr, H_q / H_kv);
 }
 
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D) {

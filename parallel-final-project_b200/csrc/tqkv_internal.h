@@ -38,11 +38,13 @@ struct AppendRows {
 
 // S rows attended per head; S_stride rows between heads in memory (0: S).
 // With `append`, K/V/scales are the cache the new rows are written into.
+// `group` query heads share one K/V head (BH counts query heads; K/V hold
+// BH / group heads); fused append needs group == 1.
 tqkv_status launch_decode(KvKind kv, OutKind out, const void* q, const void* k, const void* ks,
                           const void* v, const void* vs, void* o, int BH, int S, int D,
                           int block_size, void* workspace, size_t workspace_bytes,
                           cudaStream_t stream, int S_stride = 0,
-                          const AppendRows* append = nullptr);
+                          const AppendRows* append = nullptr, int group = 1);
 tqkv_status launch_fill_half(void* o, long long n, uint16_t bits, cudaStream_t stream);
 tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t stream);
 

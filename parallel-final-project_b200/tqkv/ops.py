@@ -174,6 +174,25 @@ def decode_int8(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.T
     return out
 
 
+def decode_int8_gqa(q: torch.Tensor, kq: torch.Tensor, ks: torch.Tensor, vq: torch.Tensor,
+                    vs: torch.Tensor, block_size: int, out: Optional[torch.Tensor] = None,
+                    workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Grouped-query decode: q [B,H_q,D] over K/V with H_kv heads ([B,H_kv,S,D]),
+    H_q a multiple of H_kv; query head h uses K/V head h // (H_q // H_kv)."""
+    B, H_kv, S, D = _bhsd(kq, "kq")
+    if q.dim() != 3 or q.shape[0] != B or q.shape[2] != D:
+        raise ValueError("q must be [B, H_q, D]")
+    H_q = q.shape[1]
+    if out is None:
+        out = torch.empty((B, H_q, D), dtype=_F16, device=q.device)
+    ws = _workspace(workspace, q.device)
+    wptr, wbytes = ws.get(workspace_bytes(B, H_q, S, D) if S > 0 else 0, stream)
+    check("tqkv_decode_int8_gqa", load().tqkv_decode_int8_gqa(
+        _ptr(q), _ptr(kq), _ptr(ks), _ptr(vq), _ptr(vs), _ptr(out), B, H_q, H_kv, S, D,
+        block_size, wptr, wbytes, _stream_handle(stream)))
+    return out
+
+
 def decode_fp16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 out: Optional[torch.Tensor] = None, workspace: Optional[Workspace] = None,
                 stream=None) -> torch.Tensor:

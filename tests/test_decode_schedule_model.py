@@ -63,9 +63,10 @@ def plan_span(src, n, lo, hi):
     return (blo, blo - a16, bhi - blo) if blo < bhi else (0, 0, 0)
 
 
-def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
+def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0, group=1):
     """T_new > 0: the fused-append variant, whose tiles get rows >= S - T_new
-    from the consumer warps' quantisation instead of the bulk copies."""
+    from the consumer warps' quantisation instead of the bulk copies.
+    group > 1: BH query heads over BH / group K/V heads (GQA)."""
     S_stride = S if S_stride is None else S_stride
     elem = 2 if half else 1
     RB = D * elem
@@ -84,8 +85,9 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
     if nchunks == 1:      # no workspace: the one chunk holds every head whole
         assert R >= total
     kbase, sbase, qbase = 1 << 40, (1 << 41) + offs[0], (1 << 42) + offs[1]
-    k_end = kbase + BH * S_stride * RB
-    s_end, q_end = sbase + BH * S_stride * nsub * 2, qbase + BH * D * 2
+    assert BH % group == 0
+    k_end = kbase + BH // group * S_stride * RB
+    s_end, q_end = sbase + BH // group * S_stride * nsub * 2, qbase + BH * D * 2
     covered = 0
     for c in range(nchunks):
         r0, r1 = c * R, min((c + 1) * R, total)
@@ -105,7 +107,7 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0):
             for t0 in tiles:
                 cnt = min(TILE, tb - t0)
                 nb = min(max(S - T_new - t0, 0), cnt) if T_new else cnt   # rows from the cache
-                row0 = bh * S_stride + t0      # memory row, as the kernel computes it
+                row0 = bh // group * S_stride + t0   # memory row, as the kernel computes it
                 assert 0 < cnt <= TILE and t0 + cnt <= S
                 assert (kbase + row0 * RB) % 16 == 0 and nb * RB % 16 == 0
                 assert kbase <= kbase + row0 * RB and kbase + (row0 + nb) * RB <= k_end
@@ -187,3 +189,11 @@ def test_schedule_in_bounds_with_fused_append(D, bs):
                                (6, 2000, 2048, 130), (3, 20000, 20001, 1), (128, 4096, 4096, 2)]:
         for offs in ((0, 0), (2, 14), (6, 2)):
             check(BH, S, D, bs, False, 4, offs, S_stride, T)
+
+
+@pytest.mark.parametrize("D,bs", [(128, 128), (128, 32), (64, 64)])
+def test_schedule_in_bounds_with_kv_groups(D, bs):
+    """GQA/MQA: query head bh reads K/V head bh // group."""
+    for BH, S, group in [(8, 1000, 4), (32, 20000, 4), (6, 257, 6), (16, 70000, 16), (4, 4097, 1)]:
+        for offs in ((0, 0), (2, 14)):
+            check(BH, S, D, bs, False, 4, offs, None, 0, group)
