@@ -65,6 +65,14 @@ __device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
     return v;
 }
 
+__device__ __forceinline__ uint2 ld_stream_v2(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(v.x), "=r"(v.y)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void st_stream_v2(uint2* p, uint2 v) {
     asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
 }
@@ -178,45 +186,44 @@ __global__ void __launch_bounds__(kCompressThreads)
 // Kernel B: y = fp16(float(code) * float(scale)).  The product of a 7-bit
 // code and an 11-bit scale is exact in fp32, so the only rounding is the
 // final fp16 conversion, as in the reference (src/kv_reconstruct.cu:33).
-// One lane owns 16 codes (one 16-byte load, two 16-byte stores); each warp
-// step loads kCompressUnroll row groups before converting any of them, so that
-// several loads per lane are in flight.
+// The codes are taken as a flat run of 8-code groups (8 divides BS and D, so
+// a group never straddles a scale block): lane l of a warp instruction reads
+// group g0 + l (8 bytes) and writes its 8 halves (16 bytes), so every load
+// covers 256 contiguous bytes and every store 512.  Each warp step issues
+// 2 * kCompressUnroll such loads per lane before converting any of them.
 template <int D, int BS>
 __global__ void __launch_bounds__(kCompressThreads)
-    kv_reconstruct_kernel(const uint4* __restrict__ xq, const __half* __restrict__ scales,
+    kv_reconstruct_kernel(const uint2* __restrict__ xq, const __half* __restrict__ scales,
                           uint4* __restrict__ y, long long rows) {
-    constexpr int kLPR = D / 16;
-    constexpr int kRPW = 32 / kLPR;
-    constexpr int kNSub = D / BS;
-    constexpr int kU = kCompressUnroll;
+    constexpr int kN = 2 * kCompressUnroll;  // group loads in flight per lane
+    static_assert(BS % 8 == 0 && D % BS == 0, "8-code groups inside scale blocks");
+    const long long n8 = rows * (D / 8);
     const int lane = threadIdx.x & 31;
-    const int c = lane % kLPR;
-    const int rsub = lane / kLPR;
     const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
-    for (long long r0 = warp * (kU * kRPW); r0 < rows; r0 += nwarps * (kU * kRPW)) {
-        uint4 raw[kU];
-        __half sh[kU];
+    for (long long g0 = warp * (32 * kN); g0 < n8; g0 += nwarps * (32 * kN)) {
+        uint2 raw[kN];
+        __half sh[kN];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const long long row = r0 + u * kRPW + rsub;
-            raw[u] = make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < kN; ++u) {
+            const long long g = g0 + u * 32 + lane;
+            raw[u] = make_uint2(0u, 0u);
             sh[u] = __ushort_as_half(0);
-            if (row < rows) {
-                raw[u] = ld_stream_v4(xq + row * kLPR + c);
-                sh[u] = scales[row * kNSub + (16 * c) / BS];
+            if (g < n8) {
+                raw[u] = ld_stream_v2(xq + g);
+                sh[u] = scales[(g * 8) / BS];
             }
         }
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const long long row = r0 + u * kRPW + rsub;
-            if (row >= rows) continue;
+        for (int u = 0; u < kN; ++u) {
+            const long long g = g0 + u * 32 + lane;
+            if (g >= n8) continue;
             const float s = __half2float(sh[u]);
-            const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-            uint32_t out[8];
+            const uint32_t w[2] = {raw[u].x, raw[u].y};
+            uint32_t out[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < 2; ++i) {
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
                     const int lo = static_cast<int8_t>((w[i] >> (16 * p)) & 0xffu);
@@ -226,8 +233,7 @@ __global__ void __launch_bounds__(kCompressThreads)
                     out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&h);
                 }
             }
-            st_stream_v4(y + (row * kLPR + c) * 2, make_uint4(out[0], out[1], out[2], out[3]));
-            st_stream_v4(y + (row * kLPR + c) * 2 + 1, make_uint4(out[4], out[5], out[6], out[7]));
+            st_stream_v4(y + g, make_uint4(out[0], out[1], out[2], out[3]));
         }
     }
 }

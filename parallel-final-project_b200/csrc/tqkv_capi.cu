@@ -206,13 +206,14 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
     if (e != cudaSuccess) return from_cuda(e);
     auto fn = kv_reconstruct_kernel<D, BS>;
     const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
-    const long long rows_per_block = (kCompressThreads / 32) * (32 / (D / 16)) * kCompressUnroll;
-    long long grid = (rows + rows_per_block - 1) / rows_per_block;
+    // one warp step covers 32 * 2 * kCompressUnroll groups of 8 codes
+    const long long groups_per_block = (kCompressThreads / 32) * 32 * 2 * kCompressUnroll;
+    long long grid = (rows * (D / 8) + groups_per_block - 1) / groups_per_block;
     const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
     return from_cuda(launch_kernel(fn, dim3(static_cast<unsigned>(grid)), dim3(kCompressThreads), 0,
-                                   stream, reinterpret_cast<const uint4*>(xq),
+                                   stream, reinterpret_cast<const uint2*>(xq),
                                    static_cast<const __half*>(scales), static_cast<uint4*>(y),
                                    rows));
 }
