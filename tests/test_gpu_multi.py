@@ -1,7 +1,8 @@
 """Split-S decode across GPUs: each rank holds a token slice of every head,
 runs the partial kernel, the records are all-gathered over NCCL and merged by
 the LSE combine kernel on every rank; and the same split over NVLink peer
-mappings (publish + combine, no NCCL) for several consecutive steps.  Both
+mappings (publish + combine, no NCCL) for several consecutive steps, also
+with the newest token appended inside the last rank's publish launch.  All
 must equal the one-GPU decode of the whole sequence.  Runs as one child process per GPU (2 to 4
 GPUs, NCCL with NVLS off); skipped when fewer than 2 GPUs are visible."""
 import datetime
@@ -63,6 +64,32 @@ def _rank_main(rank, world, port, q_out):
                 ref2 = tqkv.decode_int8(qs, kqf, ksf, vqf, vsf, w.block_size)
                 torch.cuda.synchronize()
                 err = max(err, (o2.float() - ref2.float()).abs().max().item())
+            # decode loop: the rank holding the sequence end appends each new
+            # token inside its publish launch; reference: the one-GPU fused
+            # append + decode over the whole, growing cache
+            steps, S_loc = 3, s1 - s0
+            last = rank == world - 1
+
+            def grow(t, rows):
+                c = torch.zeros(t.shape[:2] + (rows,) + t.shape[3:], dtype=t.dtype, device=dev)
+                c[:, :, :t.shape[2]] = t
+                return c
+            mine = [grow(t, S_loc + steps) for t in (kq, ks, vq, vs)]
+            whole = [grow(t, w.S + steps) for t in (kqf, ksf, vqf, vsf)]
+            gen = torch.Generator(device=dev)
+            for i in range(steps):
+                gen.manual_seed(1000 + i)
+                kn = torch.randn((w.B, w.H, 1, w.D), generator=gen, device=dev).half()
+                vn = torch.randn((w.B, w.H, 1, w.D), generator=gen, device=dev).half()
+                qs = torch.randn((w.B, w.H, w.D), generator=gen, device=dev).half()
+                if last:
+                    ex.publish_append(qs, kn, vn, *mine, S_loc + i + 1, w.block_size)
+                else:
+                    ex.publish(qs, kq, ks, vq, vs, w.block_size)
+                o3 = ex.combine(torch.empty_like(o))
+                ref3 = tqkv.decode_int8_append(qs, kn, vn, *whole, w.S + i + 1, w.block_size)
+                torch.cuda.synchronize()
+                err = max(err, (o3.float() - ref3.float()).abs().max().item())
         finally:
             ex.close()
         q_out.put((rank, err, tqkv.read_device_error()))
