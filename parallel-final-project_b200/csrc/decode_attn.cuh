@@ -10,21 +10,29 @@
 // with k_t = code_t * scale_t(block) for INT8 KV (dequantised in registers,
 // never written back).
 //
-// Work split ("flat split-S").  The B*H*S token rows are cut into equal runs
-// of R rows, one run per CTA (R = ceil(B*H*S / grid)), so every CTA streams the
-// same number of bytes whatever B, H and S are.  A run covers the tail of one
+// Work split ("flat split-S").  The B*H*S token rows, heads laid end to end,
+// are cut into fixed chunks of C rows: one chunk per CTA (C = ceil(B*H*S /
+// grid)), so every CTA streams the same number of bytes whatever B, H and S
+// are; or, when a CTA would stream very many rows, ~8 chunks per CTA that the
+// CTAs claim from a counter in the workspace.  A chunk covers the tail of one
 // head, whole heads, and the head of another; each piece ("segment") yields an
-// online-softmax state (m, l, acc[D]).  A head that lies inside one run is
-// finished by that CTA; a head cut across CTAs writes one partial per CTA to
-// the workspace and the last CTA to arrive (atomic ticket) merges them by
-// log-sum-exp and writes O.  The ticket is reset by that CTA, so the
-// workspace stays zeroed between calls.
+// online-softmax state (m, l, acc[D]).  A head that lies inside one chunk is
+// finished there; a head cut across chunks writes one partial per piece to
+// the workspace and the piece that arrives last (atomic ticket) merges them by
+// log-sum-exp and writes O.  Tickets, records and the claim counter are reset
+// by the kernel, so the workspace stays zeroed between calls.
 //
 // CTA = 4 consumer warps + 1 producer warp.  One producer lane streams tiles
 // of TILE tokens (K rows, V rows, their fp16 scales, and q at the start of a
 // segment) from HBM into a ring of STAGES shared-memory buffers with 1-D bulk
 // async copies (cp.async.bulk, mbarrier completion, L2 evict-first; no
-// multicast).  Consumers never touch global memory on the hot loop.
+// multicast), and describes each tile (head, offset, segment flags) in a
+// per-stage descriptor.  Consumers never touch global memory on the hot loop.
+//
+// Variants: OUT selects the epilogue (O, partial records, or records pushed
+// to every GPU's exchange buffer); APPEND (fused append) has the consumers
+// quantise the newest rows of each head into the cache and the tile; group > 1
+// maps query head bh to K/V head bh / group (GQA/MQA).
 //
 // Consumer mapping.  A token row is split over LPR lanes, 16 bytes each
 // (LPR = 8 for D = 128 INT8).  The LPR lanes of a "lane group" own 4 rows of
@@ -62,8 +70,8 @@ constexpr int kDecodeStages = 3;        // 3 stages x ~17.7 KB: four CTAs fit on
 enum DecodeOut : int {
     kOutHalf = 0,     // write O (fp16)
     kOutPartial = 1,  // write per-head (acc[D], m, l) records, natural-log units
-    kOutPeers = 2,    // write the records into every rank's exchange buffer, then
-                      // raise this rank's step flag on every rank (split-S over NVLink)
+    kOutPeers = 2,    // write the records, tagged with the step number, into every
+                      // rank's exchange buffer (split-S over NVLink)
 };
 
 // Exchange buffer of one rank (split-S across the GPUs of a node), written by
