@@ -9,11 +9,12 @@ from ._lib import LIB_PATH, TqkvError, load
 from .ops import (Workspace, decode_fp16, decode_int8, decode_int8_append, decode_int8_cache,
                   decode_int8_gqa, decode_int8_partial, kv_append, kv_compress, kv_reconstruct, lse_combine,
                   read_device_error, workspace_bytes)
+from .health import PeerFailure, StepMonitor
 from .peer import LocalExchange, PeerExchange
 
 __all__ = [
     "LIB_PATH", "TqkvError", "load", "Workspace", "decode_fp16", "decode_int8",
     "decode_int8_partial", "kv_compress", "kv_reconstruct", "lse_combine",
     "read_device_error", "workspace_bytes", "PeerExchange", "LocalExchange", "kv_append",
-    "decode_int8_cache", "decode_int8_append", "decode_int8_gqa",
+    "decode_int8_cache", "decode_int8_append", "decode_int8_gqa", "PeerFailure", "StepMonitor",
 ]

@@ -1,15 +1,18 @@
 """Split-S decode across the GPUs of one node over NVLink peer mappings.
 
-Each rank owns one exchange buffer (flags, step counter and double-buffered
+Each rank owns one exchange buffer (a step counter and double-buffered
 per-head records, see include/tqkv.h).  The buffers are shared with CUDA IPC
-handles, exchanged once through torch.distributed, so every rank can read
-every other rank's records and raise its step flag in every buffer.  Per
-decode step:
+handles, exchanged once through torch.distributed, so every rank can write
+into every other rank's buffer.  Per decode step:
 
-    publish(...)   decode kernel over this rank's token slice; its records go
-                   to its own buffer and its step flag to every buffer
-    combine(out)   bounded wait for every rank's flag, then every rank's
-                   records are read over NVLink and merged into O
+    publish(...)   decode kernel over this rank's token slice; each finished
+                   head's (acc, m, l) goes into every rank's buffer, every
+                   value stored together with the step number (64-bit stores)
+    combine(out)   bounded wait until this rank's buffer holds every rank's
+                   entries of this step, merge into O, advance the step
+
+A rank that stops stepping makes the others' combines time out (device error
+flag); tqkv.health.StepMonitor detects it on the host between steps.
 
 Both are plain kernel launches on the caller's stream, so a step can be
 captured in a CUDA graph.  No NCCL call and no multicast object is involved.
