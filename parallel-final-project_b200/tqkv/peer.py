@@ -26,7 +26,8 @@ import torch
 import torch.distributed as dist
 
 from ._lib import check, load
-from .ops import Workspace, _stream_handle, _workspace, workspace_bytes
+from .ops import (Workspace, _bhsd, _check_int8_kv, _need, _stream_handle, _workspace,
+                  workspace_bytes)
 
 
 class PeerExchange:
@@ -60,7 +61,10 @@ class PeerExchange:
 
     def publish(self, q, kq, ks, vq, vs, block_size: int, workspace: Optional[Workspace] = None,
                 stream=None) -> None:
-        B, H, S, D = kq.shape
+        B, H, S, D = _check_int8_kv(kq, ks, vq, vs, block_size)
+        if B * H != self.BH or D != self.D:
+            raise ValueError(f"exchange is for BH={self.BH} D={self.D}, got {B * H} x {D}")
+        _need(q, "q", B * H * D, 2, kq)
         ws = _workspace(workspace, q.device)
         wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
         check("tqkv_decode_int8_publish", load().tqkv_decode_int8_publish(
@@ -73,8 +77,15 @@ class PeerExchange:
         """publish() over the first S rows of caches [B, H, S_cap, D] after
         appending the T newest tokens (k_new / v_new fp16 [B, H, T, D]) at rows
         [S - T, S), in the same launch."""
-        B, H, S_cap, D = kq.shape
-        T = k_new.shape[2]
+        B, H, S_cap, D = _check_int8_kv(kq, ks, vq, vs, block_size)
+        if B * H != self.BH or D != self.D:
+            raise ValueError(f"exchange is for BH={self.BH} D={self.D}, got {B * H} x {D}")
+        Bn, Hn, T, Dn = _bhsd(k_new, "k_new")
+        if (Bn, Hn, Dn) != (B, H, D) or v_new.shape != k_new.shape:
+            raise ValueError("k_new and v_new must be [B, H, T, D] matching the caches")
+        for t, n in ((k_new, "k_new"), (v_new, "v_new")):
+            _need(t, n, B * H * T * D, 2, kq)
+        _need(q, "q", B * H * D, 2, kq)
         ws = _workspace(workspace, q.device)
         wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
         check("tqkv_decode_int8_append_publish", load().tqkv_decode_int8_append_publish(
@@ -83,6 +94,7 @@ class PeerExchange:
             self.bufs, self.world, self.rank, _stream_handle(stream)))
 
     def combine(self, out: torch.Tensor, stream=None) -> torch.Tensor:
+        _need(out, "out", self.BH * self.D, 2, out)
         check("tqkv_exchange_combine", load().tqkv_exchange_combine(
             self.bufs, out.data_ptr(), self.world, self.rank, self.BH, self.D,
             _stream_handle(stream)))
