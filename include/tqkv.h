@@ -16,9 +16,10 @@
  * All device pointers are owned by the caller.  All launches are
  * asynchronous on `stream`.
  *
- * Alignment contract: Kq, Vq, K and V must be 16-byte aligned (cudaMalloc and
- * torch allocations are 256-byte aligned).  Q, O, scale arrays and partials need only
- * their natural alignment.
+ * Alignment contract: Kq, Vq, K and V (and the fp16 rows of new tokens given
+ * to the append entry points) must be 16-byte aligned (cudaMalloc and torch
+ * allocations are 256-byte aligned).  Q, O, scale arrays and partials need
+ * only their natural alignment.
  */
 #ifndef TQKV_H_
 #define TQKV_H_
@@ -97,13 +98,14 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
 /* ------------------------------------------------------------------------ */
 /* Decode attention: O[b,h,:] = softmax(q . K^T / sqrt(D)) . V per (b, h).
  *
- * The B*H*S token rows are cut into fixed chunks that the CTAs claim from a
- * counter in `workspace`; a head that spans several chunks is merged by the
- * chunk that finishes it last (log-sum-exp), also in `workspace`.  Size the
- * workspace with
- * tqkv_decode_workspace_bytes() and zero it once with tqkv_workspace_init()
- * before its first use; every decode call leaves it zeroed again.  Calls that
- * share one workspace must be ordered (same stream, or events).
+ * The B*H*S token rows are cut into fixed chunks: one per CTA, or, for very
+ * long runs per CTA, about eight per CTA claimed from a counter in
+ * `workspace`.  A head that spans several chunks is merged by the chunk that
+ * finishes it last (log-sum-exp), also in `workspace`.  Size the workspace
+ * with tqkv_decode_workspace_bytes() and zero it once with
+ * tqkv_workspace_init() before its first use; every decode call leaves it
+ * zeroed again.  Calls that share one workspace must be ordered (same stream,
+ * or events).
  */
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D);
 
