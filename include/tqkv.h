@@ -109,6 +109,14 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
  */
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D);
 
+/* The decode kernels' work split for BH heads of S rows with at most
+ * `max_ctas` CTAs (the device's SMs x resident CTAs per SM): the grid, the
+ * chunk size in rows, the number of chunks, and the most pieces a head can be
+ * cut into.  Host-only (no device is touched); for capacity planning and
+ * tests. */
+tqkv_status tqkv_decode_plan(long long BH, int S, int max_ctas, long long* grid,
+                             long long* chunk_rows, long long* nchunks, long long* max_parts);
+
 tqkv_status tqkv_workspace_init(void* workspace, size_t workspace_bytes,
                                 cudaStream_t stream);
 

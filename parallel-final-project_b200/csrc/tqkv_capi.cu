@@ -601,6 +601,18 @@ tqkv_status tqkv_decode_int8_gqa(const void* q, const int8_t* kq, const void* ks
                                stream, S, nullptr, H_q / H_kv);
 }
 
+tqkv_status tqkv_decode_plan(long long BH, int S, int max_ctas, long long* grid,
+                             long long* chunk_rows, long long* nchunks, long long* max_parts) {
+    if (BH <= 0 || S <= 0 || max_ctas <= 0) return TQKV_ERR_INVALID_SIZE;
+    if (!grid || !chunk_rows || !nchunks || !max_parts) return TQKV_ERR_NULL;
+    const tqkv::DecodePlan p = tqkv::make_plan(BH, S, max_ctas);
+    *grid = p.grid;
+    *chunk_rows = p.chunk_rows;
+    *nchunks = p.nchunks;
+    *max_parts = p.max_parts;
+    return TQKV_OK;
+}
+
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D) {
     if (B <= 0 || H <= 0 || S <= 0 || (D != 64 && D != 128)) return 0;
     return tqkv::decode_workspace_bytes(static_cast<long long>(B) * H, S, D);

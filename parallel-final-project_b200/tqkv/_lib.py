@@ -59,6 +59,8 @@ C_ABI = {
                                          ctypes.POINTER(c_void_p), c_int, c_int, c_void_p]),
     "tqkv_exchange_combine": (c_int, [ctypes.POINTER(c_void_p), c_void_p, c_int, c_int, c_int,
                                       c_int, c_void_p]),
+    "tqkv_decode_plan": (c_int, [ctypes.c_longlong, c_int, c_int] +
+                         [ctypes.POINTER(ctypes.c_longlong)] * 4),
     "tqkv_decode_int8_gqa": (c_int, [c_void_p] * 6 + [c_int] * 6 + [c_void_p, c_size_t,
                                                                      c_void_p]),
     "tqkv_decode_int8_append": (c_int, [c_void_p] * 8 + [c_int] * 7 + [c_void_p, c_size_t,

@@ -197,3 +197,35 @@ def test_schedule_in_bounds_with_kv_groups(D, bs):
     for BH, S, group in [(8, 1000, 4), (32, 20000, 4), (6, 257, 6), (16, 70000, 16), (4, 4097, 1)]:
         for offs in ((0, 0), (2, 14)):
             check(BH, S, D, bs, False, 4, offs, None, 0, group)
+
+
+def _library_plan(BH, S, max_ctas):
+    import ctypes
+    from tqkv import _lib
+    lib = _lib.load()
+    out = [ctypes.c_longlong() for _ in range(4)]
+    st = lib.tqkv_decode_plan(BH, S, max_ctas, *[ctypes.byref(o) for o in out])
+    assert st == 0
+    return tuple(o.value for o in out)
+
+
+def test_model_plan_is_the_library_plan():
+    """The plan modelled here is the one the library computes (host-only
+    entry point tqkv_decode_plan, no GPU)."""
+    shapes = [(BH, S) for BH, S in SHAPES] + [(512, 8192), (128, 131072), (128, 65536),
+                                               (128, 16384), (16, 2048), (96, 1024), (1, 3)]
+    for BH, S in shapes:
+        for max_ctas in (1, 148, 296, 592, 1000):
+            assert _library_plan(BH, S, max_ctas) == make_plan(BH, S, max_ctas), (BH, S, max_ctas)
+
+
+def test_plan_entry_point_rejects_bad_arguments():
+    import ctypes
+    from tqkv import _lib
+    lib = _lib.load()
+    x = ctypes.c_longlong()
+    r = [ctypes.byref(x)] * 4
+    assert lib.tqkv_decode_plan(0, 8, 4, *r) == 2
+    assert lib.tqkv_decode_plan(4, 0, 4, *r) == 2
+    assert lib.tqkv_decode_plan(4, 8, 0, *r) == 2
+    assert lib.tqkv_decode_plan(4, 8, 4, None, *r[1:]) == 6
