@@ -229,3 +229,23 @@ def test_plan_entry_point_rejects_bad_arguments():
     assert lib.tqkv_decode_plan(4, 0, 4, *r) == 2
     assert lib.tqkv_decode_plan(4, 8, 0, *r) == 2
     assert lib.tqkv_decode_plan(4, 8, 4, None, *r[1:]) == 6
+
+
+def test_exchange_buffer_holds_every_entry():
+    """Every offset the publish epilogue writes and the combine kernel reads
+    (header words, and entry ((slot * world + rank) * BH + bh) * (D + 2) + j
+    of 8 bytes) lies inside tqkv_exchange_bytes(world, BH, D)."""
+    from tqkv import _lib
+    lib = _lib.load()
+    hdr = _const("decode_attn.cuh", "kExchangeHeaderBytes")
+    epoch, done = _const("decode_attn.cuh", "kHdrEpoch"), _const("decode_attn.cuh", "kHdrDone")
+    peers = _const("decode_attn.cuh", "kMaxPeers")
+    assert 4 * max(epoch, done) + 4 <= hdr and hdr % 16 == 0
+    for world in range(1, peers + 1):
+        for BH in (1, 7, 128, 512, 4096):
+            for D in (64, 128):
+                nbytes = lib.tqkv_exchange_bytes(world, BH, D)
+                last = hdr + (((1 * world + world - 1) * BH + BH - 1) * (D + 2) + D + 1) * 8
+                assert last + 8 <= nbytes, (world, BH, D)
+    assert lib.tqkv_exchange_bytes(peers + 1, 4, 128) == 0
+    assert lib.tqkv_exchange_bytes(2, 4, 96) == 0
