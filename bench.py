@@ -85,6 +85,23 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def decode_plan(tqkv, BH: int, S: int, device) -> dict:
+    """The decode kernel's work split for this rank's slice (host-only query
+    of the library), assuming 4 resident CTAs per SM."""
+    import ctypes
+    try:
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        out = [ctypes.c_longlong() for _ in range(4)]
+        if tqkv.load().tqkv_decode_plan(BH, S, sms * 4, *[ctypes.byref(o) for o in out]) != 0:
+            return None
+        grid, chunk, nchunks, max_parts = (o.value for o in out)
+        return {"grid": grid, "chunk_rows": chunk, "chunks": nchunks,
+                "schedule": "dynamic chunks" if nchunks > grid else "one run per CTA",
+                "max_pieces_per_head": max_parts}
+    except Exception:  # informational only
+        return None
+
+
 def traffic_per_launch(workload_name: str, n_gpus: int):
     """DRAM bytes per decode launch from the committed ncu summary
     (`traffic_bytes_per_launch <workload> <n_gpus> <bytes>` lines), or None."""
@@ -587,6 +604,7 @@ def main():
                             f"split-S x{world} + NCCL all-gather" if collective else
                             f"B*H shards x{world}, no collective" if world > 1 else "1 GPU"),
             "cuda_graphs": bool(graphs_used),
+            "decode_plan": decode_plan(tqkv, BH_loc, S_loc, dev) if S_loc > 0 else None,
             "l2": (f"KV {local_bytes / 1e6:.1f} MB per GPU per step >= 2x the "
                    f"{l2_bytes / 1e6:.0f} MB L2; no flush needed" if flush_buf is None else
                    f"KV {local_bytes / 1e6:.1f} MB per GPU per step < 2x the {l2_bytes / 1e6:.0f} "
