@@ -595,7 +595,7 @@ def main():
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "int8 codes, s32 dp4a K-dot, fp32 softmax/V",
+        "dtype": "int8",
         "data": f"synthetic, generated on device: {w.description}",
         "config": {
             "workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D,
@@ -603,6 +603,7 @@ def main():
             "parallelism": (f"split-S x{world} + NVLink peer exchange" if use_p2p else
                             f"split-S x{world} + NCCL all-gather" if collective else
                             f"B*H shards x{world}, no collective" if world > 1 else "1 GPU"),
+            "arithmetic": "int8 codes; K-dot in s32 (dp4a); softmax and V accumulation in fp32",
             "cuda_graphs": bool(graphs_used),
             "decode_plan": decode_plan(tqkv, BH_loc, S_loc, dev) if S_loc > 0 else None,
             "l2": (f"KV {local_bytes / 1e6:.1f} MB per GPU per step >= 2x the "
