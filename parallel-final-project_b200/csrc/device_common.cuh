@@ -85,12 +85,6 @@ __device__ __forceinline__ uint64_t make_evict_first_policy() {
     return policy;
 }
 
-__device__ __forceinline__ uint64_t make_evict_last_policy() {
-    uint64_t policy;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
-    return policy;
-}
-
 // 1-D bulk async copy global -> this CTA's shared memory, completing `bytes`
 // of transaction count on `bar`.  dst, src and bytes must be multiples of 16.
 // No multicast: the source is always this GPU's own memory.
@@ -101,31 +95,6 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
-}
-
-// System-scope release store / acquire load of a 32-bit flag (peer GPUs
-// read and write these through NVLink peer mappings).
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Wait until *flag (a step counter) reaches `target`, with the same hard
-// bound as mbar_wait_bounded.  Wrap-safe comparison.
-__device__ __forceinline__ bool wait_flag_bounded(const unsigned int* flag, unsigned int target) {
-    if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
-    const long long start = clock64();
-#pragma unroll 1
-    for (uint32_t it = 0; it < (1u << 30); ++it) {
-        if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
-        if (clock64() - start > (1ll << 31)) break;
-        __nanosleep(64);
-    }
-    return false;
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
