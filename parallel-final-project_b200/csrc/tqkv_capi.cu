@@ -234,9 +234,11 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
 
     const DecodePlan bound = bound_plan(BH, S, dev);
     const WsLayout lay = ws_layout(BH, bound.max_parts, D);
-    const long long resident = static_cast<long long>(sm_count(dev)) * per_sm;
+    // the workspace bound covers up to kMaxCtasPerSmBound CTAs per SM
+    const int occ = per_sm < kMaxCtasPerSmBound ? per_sm : kMaxCtasPerSmBound;
+    const long long resident = static_cast<long long>(sm_count(dev)) * occ;
     const DecodePlan plan = make_plan(BH, S, resident);
-    if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: per_sm <= bound
+    if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: occ <= bound
     // records and tickets for cut heads; the claim counter for dynamic chunks
     const bool needs_ws = plan.nchunks > 1;
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
