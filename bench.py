@@ -72,7 +72,24 @@ def parse_args():
                    help="skip the CPU baseline leg (rank 0, N=1)")
     p.add_argument("--cpu-budget-s", type=float, default=20.0,
                    help="host seconds for the CPU baseline sample")
+    p.add_argument("--csv", default=None,
+                   help="also append a row in the reference bench's CSV schema "
+                        "(src/benchmark.cpp:109) plus gpus, eff_GBps, pct_peak (rank 0)")
     return p.parse_args()
+
+
+CSV_HEADER = ("mode,B,H,D,S,block_size,iters,attn_us,reconstruct_us,compress_us,total_us,"
+              "std_us,min_us,bytes_kv,tile_n,lanes_per_thread,gpus,eff_GBps,pct_peak")
+
+
+def append_csv(path: str, row: dict) -> None:
+    """One row of the reference bench's CSV (same columns, same meaning; the
+    tile and lane knobs do not apply and are 0) with three added columns."""
+    new = not os.path.exists(path) or os.path.getsize(path) == 0
+    with open(path, "a") as f:
+        if new:
+            f.write(CSV_HEADER + "\n")
+        f.write(",".join(str(row[c]) for c in CSV_HEADER.split(",")) + "\n")
 
 
 def measured_peaks():
@@ -518,6 +535,7 @@ def main():
     else:
         step_ms_local = statistics.mean(a.elapsed_time(c) for a, _, c in kev)
     kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    step_samples_ms = [a.elapsed_time(c) for a, _, c in kev]   # per step, this rank
     hot_ms_local = step_ms_local
     if flush_buf is not None:     # the same steps back to back, KV left in L2
         torch.cuda.synchronize()
@@ -642,6 +660,16 @@ def main():
         "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
+    if args.csv:
+        append_csv(args.csv, {
+            "mode": "int8_fused_online", "B": w.B, "H": w.H, "D": w.D, "S": w.S,
+            "block_size": w.block_size, "iters": args.steps, "attn_us": step_ms * 1e3,
+            "reconstruct_us": 0, "compress_us": statistics.mean(comp_us),
+            "total_us": step_ms * 1e3,
+            "std_us": statistics.pstdev(step_samples_ms) * 1e3,
+            "min_us": min(step_samples_ms) * 1e3, "bytes_kv": total_bytes, "tile_n": 0,
+            "lanes_per_thread": 0, "gpus": world, "eff_GBps": value,
+            "pct_peak": 100.0 * value / world / NOMINAL_HBM_GBS})
     return 0
 
 
