@@ -7,6 +7,7 @@ out step after step, each leaving an error code in the device flag and a
 meaningless O.  StepMonitor catches that on the host, between steps, before
 any kernel of the next step is launched:
 
+    monitor.start()                       # every rank is set up
     for step in range(n):
         monitor.wait_peers(step - 1)      # every peer finished the previous step
         exchange.publish(...); exchange.combine(out)
@@ -54,6 +55,24 @@ class StepMonitor:
         if not self.store.check([key]):
             return None
         return self.store.get(key).decode()
+
+    def start(self, timeout_s: float = 120.0) -> None:
+        """Barrier before the first step, so that set-up time (which differs
+        between ranks) does not count against the step deadline.  Raises
+        PeerFailure naming a rank that has not arrived after `timeout_s`."""
+        self.store.set(self._key("started", self.rank), "1")
+        t0 = time.monotonic()
+        pending = [r for r in range(self.world) if r != self.rank]
+        while pending:
+            pending = [r for r in pending if self._read("started", r) is None]
+            for r in pending:
+                reason = self._read("failed", r)
+                if reason is not None:
+                    raise PeerFailure(r, -1, reason, time.monotonic() - t0)
+            if pending and time.monotonic() - t0 > timeout_s:
+                raise PeerFailure(pending[0], -1, None, time.monotonic() - t0)
+            if pending:
+                time.sleep(self.poll_s)
 
     def finished(self, step: int) -> None:
         """This rank has completed `step` (its O is on the host)."""

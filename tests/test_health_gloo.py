@@ -29,11 +29,7 @@ def _worker(rank, world, port, scenario, deadline, out):
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
                           timeout=datetime.timedelta(seconds=30))
     mon = StepMonitor(store, rank, world, deadline_s=deadline)
-    # start together: process start-up skew is not a stopped rank
-    store.add("start", 1)
-    end = time.monotonic() + 120
-    while int(store.add("start", 0)) < world and time.monotonic() < end:
-        time.sleep(0.01)
+    mon.start()   # set-up (process start) time does not count against the deadline
     result = ("ok", None, None, None, None)
     t_wait = time.monotonic()
     try:
@@ -105,3 +101,39 @@ def test_monitor_validates_rank():
     from tqkv.health import StepMonitor
     with pytest.raises(ValueError):
         StepMonitor(None, 3, 3)
+
+
+def _start_worker(rank, world, port, out):
+    import sys
+    sys.path.insert(0, os.path.join(REPO, "parallel-final-project_b200"))
+    from tqkv.health import PeerFailure, StepMonitor
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=30))
+    mon = StepMonitor(store, rank, world)
+    res = ("ok", None)
+    if rank != world - 1:          # the last rank never starts
+        try:
+            mon.start(timeout_s=1.0)
+        except PeerFailure as e:
+            res = ("peer_failure", e.rank)
+    out.put((rank,) + res)
+    store.set(f"exit/{rank}", "1")
+    if rank == 0:
+        end = time.monotonic() + 20
+        while time.monotonic() < end and not store.check([f"exit/{r}" for r in range(world)]):
+            time.sleep(0.01)
+
+
+def test_start_reports_a_rank_that_never_arrives():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_start_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=60) for _ in range(3))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][1:] == ("peer_failure", 2) and res[1][1:] == ("peer_failure", 2)
+    assert res[2][1:] == ("ok", None)
