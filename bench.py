@@ -138,7 +138,7 @@ def traffic_per_launch(workload_name: str, n_gpus: int):
 # NVML sampling loop, run in a child process so that it keeps sampling while
 # the benchmark's main thread sits in CUDA calls (which can hold the GIL when
 # the launch queue is full).  Prints "ready", then one line per sample:
-# "sm_mhz mem_mhz power_mw reasons_mask", until its stdin closes.
+# "monotonic_s sm_mhz mem_mhz power_mw reasons_mask", until its stdin closes.
 _SAMPLER_SRC = r"""
 import sys, threading, time
 import pynvml
@@ -150,7 +150,7 @@ threading.Thread(target=lambda: (sys.stdin.read(), stop.set()), daemon=True).sta
 print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
 while not stop.is_set():
     try:
-        print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+        print(time.monotonic(), pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
               pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_MEM),
               pynvml.nvmlDeviceGetPowerUsage(h),
               pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
@@ -177,6 +177,13 @@ class ClockSampler:
         self.max_mhz = None
         self.device_index, self.interval = device_index, interval_s
         self.proc = None
+        self.window = [None, None]   # host monotonic times bracketing the timed region
+
+    def mark_start(self):
+        self.window[0] = time.monotonic()
+
+    def mark_end(self):
+        self.window[1] = time.monotonic()
 
     def __enter__(self):
         import subprocess
@@ -199,11 +206,19 @@ class ClockSampler:
         if self.proc is None:
             return
         out, _ = self.proc.communicate(input="", timeout=30)
+        rows = []
         for line in out.splitlines():
             f = line.split()
-            if len(f) != 4:
+            if len(f) != 5:
                 continue
-            sm, mem, mw, mask = (int(x) for x in f)
+            rows.append((float(f[0]),) + tuple(int(x) for x in f[1:]))
+        # keep the samples taken while the timed region ran (the sampler also
+        # runs through the barrier before it, when the GPU may sit idle)
+        t0, t1 = self.window
+        if t0 is not None and t1 is not None:
+            inside = [r for r in rows if t0 <= r[0] <= t1]
+            rows = inside if inside else rows
+        for _, sm, mem, mw, mask in rows:
             self.samples.append(sm)
             self.mem_mhz.append(mem)
             self.power_w.append(mw / 1000.0)
@@ -344,6 +359,78 @@ def kernel_table(w, tqkv, kq, ks, vq, vs, q, comp_us, ws, reps: int = 5):
     del k16, v16
     torch.cuda.empty_cache()
     return out
+
+
+
+def timing_check(step_ms: float, e2e_ms: float, comparable: bool) -> str:
+    """The device-timed step must not be slower than the end-to-end step,
+    which does the same work plus copies and a host sync every step."""
+    if not comparable:
+        return "n/a (L2 overwritten before each device-timed step, not before e2e steps)"
+    if step_ms <= e2e_ms * 1.02:
+        return "ok: device step <= e2e step"
+    msg = (f"device step {step_ms * 1e3:.1f} us > e2e step {e2e_ms * 1e3:.1f} us: "
+           "the device timing includes waits that are not the step")
+    print("bench: " + msg, file=sys.stderr, flush=True)
+    return "FAILED: " + msg
+
+
+PARITY_TOL = 1e-3
+
+
+def multi_gpu_parity(w, tqkv, out, shard: str, rank: int, world: int, h0: int, dev):
+    """O of the multi-GPU step (every rank's, gathered to rank 0) against the
+    one-GPU decode of a sample of heads over the whole sequence.  The
+    reference's codes are compressed here from the workload's generator, so
+    this also checks that every rank's slice holds the right tokens.  Split-S
+    ranks all merge the same records in the same order, so their O must be
+    bit-identical.  Returns a dict on rank 0 (None elsewhere)."""
+    import torch.distributed as dist
+    from tqkv import workloads as W
+    mine = out.view(-1, w.D).cpu()
+    gathered = [None] * world
+    dist.all_gather_object(gathered, (rank, h0, mine))
+    if rank != 0:
+        return None
+    BH, D = w.BH, w.D
+    if shard == "s":
+        full = gathered[0][2]
+        identical = all(torch.equal(g[2], full) for g in gathered)
+        heads = sorted({0, BH // 3, (2 * BH) // 3, BH - 1})
+    else:
+        full = torch.empty((BH, D), dtype=torch.float16)
+        heads = []
+        for _, hh0, o in gathered:
+            full[hh0:hh0 + o.shape[0]] = o
+            if o.shape[0]:
+                heads += [hh0, hh0 + o.shape[0] - 1]
+        heads = sorted(set(heads))
+        identical = None
+    nh = len(heads)
+    idx = torch.tensor(heads, device=dev)
+    codes = []
+    for which in ("k", "v"):
+        xq = torch.empty((1, nh, w.S, D), dtype=torch.int8, device=dev)
+        xs = torch.empty((1, nh, w.S, D // w.block_size), dtype=torch.float16, device=dev)
+        for t0 in range(0, w.S, W.CHUNK):
+            t1 = min(t0 + W.CHUNK, w.S)
+            x = W.make_kv_slice(w, which, t0, t1, dev).reshape(BH, t1 - t0, D)
+            x = x.index_select(0, idx).reshape(1, nh, t1 - t0, D).contiguous()
+            cq, cs = tqkv.kv_compress(x, w.block_size)
+            xq[:, :, t0:t1] = cq
+            xs[:, :, t0:t1] = cs
+            del x, cq, cs
+        codes += [xq, xs]
+    q = W.make_q(w, dev).reshape(BH, D).index_select(0, idx).reshape(1, nh, D).contiguous()
+    ref = tqkv.decode_int8(q, *codes, w.block_size).reshape(nh, D).cpu()
+    got = full.index_select(0, torch.tensor(heads))
+    err = float((got.float() - ref.float()).abs().max())
+    finite = bool(torch.isfinite(got.float()).all())
+    ok = finite and err <= PARITY_TOL and identical is not False
+    return {"max_abs": err, "tol": PARITY_TOL, "heads": heads, "ok": ok,
+            "ranks_bit_identical": identical,
+            "reference": "one-GPU tqkv_decode_int8 over the whole sequence of the sampled "
+                         "heads, codes compressed here from the workload generator"}
 
 
 def main():
@@ -511,11 +598,21 @@ def main():
                  if local_bytes < 2 * l2_bytes else None)
 
     # ---- timed region: exactly K steps ----
+    # The clock sampler starts before the barrier: it spawns a process, and
+    # host-side work between the barrier and the first timed launch would
+    # land inside the other ranks' timed regions (their combines wait for this
+    # rank).  After the barrier one untimed step goes first, with no host sync
+    # between it and the timed steps: every rank's combine ends only once all
+    # ranks have published that step, so whatever host skew the ranks leave
+    # the barrier with is absorbed there and the timed regions start together.
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
            for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
+        run_kernel()
+        run_comm()
         torch.cuda.nvtx.range_push("tqkv_timed")  # lets ncu --nvtx-include select this region
         ev0.record()
         for i in range(args.steps):
@@ -529,6 +626,7 @@ def main():
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
+        clk.mark_end()
     barrier()
     if flush_buf is None:
         step_ms_local = ev0.elapsed_time(ev1) / args.steps
@@ -536,10 +634,16 @@ def main():
         step_ms_local = statistics.mean(a.elapsed_time(c) for a, _, c in kev)
     kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
     step_samples_ms = [a.elapsed_time(c) for a, _, c in kev]   # per step, this rank
+    # step-to-step period (start of one step to the start of the next)
+    period_ms_local = (statistics.median(kev[i][0].elapsed_time(kev[i + 1][0])
+                                         for i in range(args.steps - 1))
+                       if args.steps > 1 and flush_buf is None else step_ms_local)
     hot_ms_local = step_ms_local
     if flush_buf is not None:     # the same steps back to back, KV left in L2
         torch.cuda.synchronize()
         barrier()
+        run_kernel()
+        run_comm()
         ev0.record()
         for i in range(args.steps):
             run_kernel()
@@ -557,6 +661,8 @@ def main():
         torch.cuda.current_stream().synchronize()
     barrier()
     torch.cuda.synchronize()
+    run_e2e()          # aligns the ranks, as before the timed region above
+    torch.cuda.current_stream().synchronize()
     ev0.record()
     for _ in range(e2e_steps):
         run_e2e()
@@ -573,11 +679,16 @@ def main():
         kernels = kernel_table(w, tqkv, kq, ks, vq, vs, q, comp_us, ws)
 
     # ---- max over ranks ----
-    t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, hot_ms_local, float(err)],
-                     device=dev)
+    t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, hot_ms_local, float(err),
+                      period_ms_local], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, kern_ms, e2e_ms, hot_ms, err_max = t.tolist()
+    step_ms, kern_ms, e2e_ms, hot_ms, err_max, period_ms = t.tolist()
+
+    # ---- multi-GPU parity: O against the one-GPU decode of sampled heads ----
+    parity = None
+    if world > 1:
+        parity = multi_gpu_parity(w, tqkv, out, shard, rank, world, h0, dev)
 
     total_bytes = w.kv_bytes_int8()
     peak, peak_kind = measured_peaks()
@@ -657,6 +768,10 @@ def main():
             "us_per_step": hot_ms * 1e3, "GBps": total_bytes / (hot_ms * 1e-3) / 1e9,
             "note": "same steps back to back, KV resident in L2"},
         "device_error": int(err_max),
+        "step_period_us_median": period_ms * 1e3,
+        "timing_check": timing_check(step_ms, e2e_ms, flush_buf is None),
+        "parity_max_abs": None if parity is None else parity["max_abs"],
+        "parity": parity,
         "kernels": kernels,
     }
     print(json.dumps(line), flush=True)
@@ -670,6 +785,13 @@ def main():
             "min_us": min(step_samples_ms) * 1e3, "bytes_kv": total_bytes, "tile_n": 0,
             "lanes_per_thread": 0, "gpus": world, "eff_GBps": value,
             "pct_peak": 100.0 * value / world / NOMINAL_HBM_GBS})
+    if parity is not None and not parity["ok"]:
+        print(f"bench: multi-GPU output differs from the one-GPU decode: {parity}",
+              file=sys.stderr, flush=True)
+        return 1
+    if int(err_max) != 0:
+        print(f"bench: device error code {int(err_max)}", file=sys.stderr, flush=True)
+        return 1
     return 0
 
 

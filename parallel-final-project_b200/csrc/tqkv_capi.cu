@@ -22,6 +22,7 @@
 #include "kv_compress.cuh"
 #include "tqkv.h"
 #include "tqkv_internal.h"
+#include "ws_cache.h"
 
 #ifndef TQKV_COMPRESS_DIV_MODE
 // Division form used by Kernel A.  The reference is built with
@@ -444,12 +445,25 @@ size_t decode_workspace_bytes(long long BH, int S, int D) {
 }
 
 namespace {
-struct CachedWs {
-    void* ptr = nullptr;
-    size_t bytes = 0;
+// cudaMalloc + zero fill in stream order; the failing call's error is kept
+// for the calling thread (tqkv_last_cuda_error).
+struct CudaZeroedAlloc {
+    void* operator()(int /*device: current*/, cudaStream_t stream, size_t bytes) const {
+        void* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, bytes, stream);
+        if (e != cudaSuccess) {
+            if (p) cudaFree(p);
+            from_cuda(e);
+            return nullptr;
+        }
+        return p;
+    }
 };
-std::mutex g_ws_mu;
-std::map<std::pair<int, cudaStream_t>, CachedWs> g_ws;
+WorkspaceCache<cudaStream_t, CudaZeroedAlloc>& ws_cache() {
+    static WorkspaceCache<cudaStream_t, CudaZeroedAlloc> cache{CudaZeroedAlloc{}};
+    return cache;
+}
 }  // namespace
 
 void* cached_workspace(cudaStream_t stream, size_t bytes, tqkv_status* status) {
@@ -461,30 +475,8 @@ void* cached_workspace(cudaStream_t stream, size_t bytes, tqkv_status* status) {
         *status = from_cuda(e);
         return nullptr;
     }
-    std::lock_guard<std::mutex> lock(g_ws_mu);
-    CachedWs& c = g_ws[{dev, stream}];
-    if (c.bytes >= bytes) return c.ptr;
-    if (c.ptr) {
-        // the old buffer may still be in use by work queued on this stream
-        e = cudaStreamSynchronize(stream);
-        if (e == cudaSuccess) e = cudaFree(c.ptr);
-        c.ptr = nullptr;
-        c.bytes = 0;
-        if (e != cudaSuccess) {
-            *status = from_cuda(e);
-            return nullptr;
-        }
-    }
-    void* p = nullptr;
-    e = cudaMalloc(&p, bytes);
-    if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, bytes, stream);
-    if (e != cudaSuccess) {
-        if (p) cudaFree(p);
-        *status = from_cuda(e);
-        return nullptr;
-    }
-    c.ptr = p;
-    c.bytes = bytes;
+    void* p = ws_cache().get(dev, stream, bytes);
+    if (p == nullptr) *status = TQKV_ERR_CUDA;
     return p;
 }
 

@@ -55,8 +55,10 @@ size_t decode_workspace_bytes(long long BH, int S, int D);
 size_t decode_ws_counter_bytes(long long BH);
 
 // Per-(device, stream) grow-only workspace used by the reference-signature
-// launchers, which have no workspace argument.  Zero-filled on allocation
-// (the kernels keep it zeroed).  Mutex-guarded; returns nullptr on failure.
+// launchers, which have no workspace argument (ws_cache.h).  Zero-filled on
+// allocation (the kernels keep it zeroed); a buffer once handed out is never
+// freed, so a launch enqueued after another thread grew the cache still runs
+// on valid memory.  Mutex-guarded; returns nullptr on failure.
 void* cached_workspace(cudaStream_t stream, size_t bytes, tqkv_status* status);
 
 // Sets cudaErrorInvalidConfiguration as the pending launch error, exactly as

@@ -3,7 +3,9 @@
 `torch_attention_fp32`), run on the seeded inputs of gen.py.
 
 Run where the reference is mounted (not on the GPU box):
-    python tests/golden/make_golden_python.py [/root/reference]
+    python tests/golden/make_golden_python.py [REFERENCE_ROOT]
+REFERENCE_ROOT defaults to $TQKV_REF_ROOT, else a checkout named `reference`
+beside this repository.
 The codes fed to `dequantize` come from the CPU oracle's compress (any valid
 codes pin the dequantise/attention formulas; the codes themselves are pinned
 separately by ref_build_golden.json).
@@ -24,7 +26,8 @@ from oracle import oracle as O  # noqa: E402
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = (sys.argv[1] if len(sys.argv) > 1 else
+                os.environ.get("TQKV_REF_ROOT", os.path.join(os.path.dirname(REPO), "reference")))
     spec = importlib.util.spec_from_file_location(
         "check_correctness", os.path.join(ref_root, "python", "check_correctness.py"))
     cc = importlib.util.module_from_spec(spec)

@@ -113,7 +113,10 @@ def _start_worker(rank, world, port, out):
     res = ("ok", None)
     if rank != world - 1:          # the last rank never starts
         try:
-            mon.start(timeout_s=1.0)
+            # long enough that start-up skew between the two live ranks (a
+            # loaded host can take a second or more to get a spawned child
+            # past the store) is not taken for a missing rank
+            mon.start(timeout_s=5.0)
         except PeerFailure as e:
             res = ("peer_failure", e.rank)
     out.put((rank,) + res)

@@ -8,8 +8,10 @@ them the library carries a fixed scratch array in its own device memory
 
 These tests call it through the C ABI (ctypes) twice in a row and compare
 each result with the workspace-taking entry point tqkv_decode_int8 on the
-same inputs, within the tolerance the decode tests use; they also check that a
-shape too large for the array is refused.  This file is collected last, and
+same inputs.  Both run the same kernel with the same work split and merge
+order, so the outputs must be bit-identical (a stricter check than the decode
+tests' tolerance, which is asserted as well); they also check that a shape too
+large for the array is refused.  This file is collected last, and
 it passes both on its own in a fresh process and after the other tests.
 """
 import ctypes
@@ -64,6 +66,7 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
         assert _noalloc(q, kq, ks, vq, vs, o, bs) == TQKV_OK
         ref = tqkv.decode_int8(q, kq, ks, vq, vs, bs)   # the existing entry point
         torch.cuda.synchronize()
+        assert torch.equal(o, ref), i
         assert _within_decode_tolerance(o, ref), i
     assert tqkv.read_device_error() == 0
 
@@ -80,7 +83,8 @@ def test_noalloc_repeated_call_same_inputs():
     assert _noalloc(q, kq, ks, vq, vs, o2, bs) == TQKV_OK
     ref = tqkv.decode_int8(q, kq, ks, vq, vs, bs)
     torch.cuda.synchronize()
-    assert _within_decode_tolerance(o1, ref) and _within_decode_tolerance(o2, ref)
+    assert torch.equal(o1, ref) and torch.equal(o2, ref)
+    assert _within_decode_tolerance(o1, ref)
 
 
 def test_noalloc_refuses_shapes_beyond_the_array():
