@@ -65,9 +65,11 @@ def parse_args():
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     p.add_argument("--no-kernel-table", action="store_true",
                    help="skip the per-kernel measurements of compress / reconstruct / fp16 decode")
-    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
-                   help="split-S record exchange: NVLink peer writes + bounded-wait combine "
-                        "(p2p), or NCCL all-gather + combine kernel (nccl, never graph-captured)")
+    p.add_argument("--exchange", choices=["p2p", "p2p2", "nccl"], default="p2p",
+                   help="split-S record exchange: NVLink peer writes and the bounded-wait "
+                        "merge in the decode launch itself (p2p, one cooperative launch per "
+                        "step), the same as two launches, decode then combine (p2p2), or NCCL "
+                        "all-gather + combine kernel (nccl, never graph-captured)")
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU baseline leg (rank 0, N=1)")
     p.add_argument("--cpu-budget-s", type=float, default=20.0,
@@ -495,13 +497,16 @@ def main():
     out = torch.empty((1, BH_loc, D), dtype=torch.float16, device=dev)
     ws = tqkv.Workspace(dev)
     collective = world > 1 and shard == "s"
-    use_p2p = collective and args.exchange == "p2p"
+    use_p2p = collective and args.exchange in ("p2p", "p2p2")
+    one_launch = use_p2p and args.exchange == "p2p"
     local_rec = torch.empty((BH, D + 2), dtype=torch.float32, device=dev)
     gathered = torch.empty((world, BH, D + 2), dtype=torch.float32, device=dev)
     exchange = tqkv.PeerExchange(world, rank, BH, D) if use_p2p else None
 
     def kernel():
-        if use_p2p:
+        if one_launch:
+            exchange.step(q, kq, ks, vq, vs, w.block_size, out, workspace=ws)
+        elif use_p2p:
             exchange.publish(q, kq, ks, vq, vs, w.block_size, workspace=ws)
         elif collective:
             tqkv.decode_int8_partial(q, kq, ks, vq, vs, w.block_size, out=local_rec, workspace=ws)
@@ -509,6 +514,8 @@ def main():
             tqkv.decode_int8(q, kq, ks, vq, vs, w.block_size, out=out, workspace=ws)
 
     def comm():
+        if one_launch:
+            return                   # merged inside the step's launch
         if use_p2p:
             exchange.combine(out)
         elif collective:
@@ -541,9 +548,14 @@ def main():
         if owns_last and not collective:      # append fused into the decode launch
             tqkv.decode_int8_append(q, kv_new[0], kv_new[1], kq, ks, vq, vs, S_loc,
                                     w.block_size, out=out, workspace=ws)
+        elif owns_last and one_launch:
+            exchange.step_append(q, kv_new[0], kv_new[1], kq, ks, vq, vs, S_loc,
+                                 w.block_size, out, workspace=ws)
         elif owns_last and use_p2p:
             exchange.publish_append(q, kv_new[0], kv_new[1], kq, ks, vq, vs, S_loc,
                                     w.block_size, workspace=ws)
+        elif one_launch:
+            exchange.step(q, kq, ks, vq, vs, w.block_size, out, workspace=ws)
         else:
             if owns_last:                     # NCCL path: separate append launches
                 tqkv.kv_append(kv_new[0], kq, ks, S_loc - 1, w.block_size)
@@ -571,15 +583,16 @@ def main():
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         captured = []
-        for fn in ((kernel, comm, e2e_step) if collective else (kernel, e2e_step)):
+        two_part = collective and not one_launch
+        for fn in ((kernel, comm, e2e_step) if two_part else (kernel, e2e_step)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
             graphs.append(g)
             captured.append(g.replay)
-        if collective:
+        if two_part:
             run_kernel, run_comm, run_e2e = captured
-        else:                   # one GPU: nothing to exchange
+        else:                   # one launch per step: nothing else to run
             (run_kernel, run_e2e), run_comm = captured, comm
     else:
         run_kernel, run_comm, run_e2e = kernel, comm, e2e_step
@@ -729,7 +742,10 @@ def main():
         "config": {
             "workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D,
             "block_size": w.block_size, "global_batch": w.B, "seq_len": w.S,
-            "parallelism": (f"split-S x{world} + NVLink peer exchange" if use_p2p else
+            "parallelism": (f"split-S x{world} + NVLink peer exchange, one launch per step"
+                            if one_launch else
+                            f"split-S x{world} + NVLink peer exchange, decode + combine launches"
+                            if use_p2p else
                             f"split-S x{world} + NCCL all-gather" if collective else
                             f"B*H shards x{world}, no collective" if world > 1 else "1 GPU"),
             "arithmetic": "int8 codes; K-dot in s32 (dp4a); softmax and V accumulation in fp32",
@@ -742,7 +758,10 @@ def main():
                    f"timed step, outside the step's events"),
         },
         "roofline": {
-            "bound": "hbm", "kernel": DECODE_KERNEL + (" (split-S partial)" if collective else ""),
+            "bound": "hbm",
+            "kernel": DECODE_KERNEL + (" (split-S, records exchanged and merged in the launch)"
+                                       if one_launch else
+                                       " (split-S partial)" if collective else ""),
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": peak_kind, "traffic": traffic,
             "algorithmic_bytes_per_launch": local_bytes, "launch_ms": kern_ms,
@@ -756,10 +775,15 @@ def main():
                 "step": "H2D q, k_new, v_new (pinned) -> " +
                         ("append k, v to the int8 cache (separate launches) -> decode"
                          if collective and not use_p2p else
+                         "decode with the append of k, v, the record exchange and the merge "
+                         "fused in one launch (tqkv_decode_int8_append_exchange on the rank "
+                         "holding the newest tokens, tqkv_decode_int8_exchange elsewhere)"
+                         if one_launch else
                          "decode with the append of k, v fused in (tqkv_decode_int8_append" +
                          ("_publish on the rank holding the newest tokens)" if collective else ")")) +
-                        (" -> exchange + combine" if collective else "") + " -> D2H O -> host sync"},
-        "gpu_launches": args.steps * (2 if collective else 1),
+                        (" -> exchange + combine" if collective and not one_launch else "") +
+                        " -> D2H O -> host sync"},
+        "gpu_launches": args.steps * (2 if collective and not one_launch else 1),
         "clocks": clk.summary(),
         "compress": {"us_per_tensor": statistics.mean(comp_us),
                      "GBps": (w.BH * S_loc * w.D * 3 + w.BH * S_loc * (w.D // w.block_size) * 2)

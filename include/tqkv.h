@@ -100,12 +100,15 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
  *
  * The B*H*S token rows are cut into fixed chunks: one per CTA, or, for very
  * long runs per CTA, about eight per CTA claimed from a counter in
- * `workspace`.  A head that spans several chunks is merged by the chunk that
- * finishes it last (log-sum-exp), also in `workspace`.  Size the workspace
- * with tqkv_decode_workspace_bytes() and zero it once with
- * tqkv_workspace_init() before its first use; every decode call leaves it
- * zeroed again.  Calls that share one workspace must be ordered (same stream,
- * or events).
+ * `workspace`.  A head that spans several chunks leaves one record per piece
+ * in `workspace`; the CTA that streamed its first piece merges them
+ * (log-sum-exp, in piece order: results do not depend on which CTA streamed
+ * which chunk) once it has streamed all of its own chunks.  Kernel launches
+ * are cooperative (every CTA resident).  Size the workspace with
+ * tqkv_decode_workspace_bytes() and zero it once with tqkv_workspace_init()
+ * before its first use; every decode call leaves it zeroed again (after a
+ * device error, zero it again).  Calls that share one workspace must be
+ * ordered (same stream, or events).
  */
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D);
 
@@ -226,7 +229,8 @@ tqkv_status tqkv_lse_combine(const float* partials, void* o,
  *   tqkv_decode_int8_publish  computes this rank's per-head records
  *       (acc[D], m, l) over its token slice and stores them into every rank's
  *       buffer through the peer mappings; each value travels with the step
- *       number in one 64-bit store, so no fence or flag is needed;
+ *       number in one 64-bit store, so no fence or flag is needed (S == 0:
+ *       empty records, m = -inf, l = 0, acc = 0);
  *   tqkv_exchange_combine     waits (bounded, ~1 s) until every rank's
  *       entries of this step have arrived in this rank's buffer, merges them
  *       into O and advances this rank's step counter.
@@ -264,6 +268,39 @@ tqkv_status tqkv_decode_int8_append_publish(const void* q,
 tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o,
                                   int world, int rank, int BH, int D, cudaStream_t stream);
 
+/* One split-S decode step in ONE launch: the work of tqkv_decode_int8_publish
+ * followed by that of tqkv_exchange_combine, O (fp16 [B,H,D]) out.  After its
+ * share of the token slice, each CTA takes heads from a counter in the
+ * workspace, waits (bounded, ~1 s) for every rank's records of the head,
+ * merges them and writes O; the last CTA to finish advances this rank's step
+ * counter.  The launch is cooperative (every CTA resident), because a CTA may
+ * wait for records that another CTA of the same launch emits.  Same O as the
+ * two-launch pair, bit for bit, with the same buffers and record slots: a
+ * sequence of steps may use either form, step by step.  S == 0 (a rank whose
+ * slice is empty) publishes empty records and merges with two small launches.
+ * A wait that runs out leaves NaN in that head's O and sets the device error
+ * flag; after a device error, re-zero the workspace (tqkv_workspace_init) and
+ * the exchange buffers before further steps. */
+tqkv_status tqkv_decode_int8_exchange(const void* q,
+                                      const int8_t* kq, const void* ks,
+                                      const int8_t* vq, const void* vs,
+                                      void* o,
+                                      int B, int H, int S, int D, int block_size,
+                                      void* workspace, size_t workspace_bytes,
+                                      void* const* exchange_bufs, int world, int rank,
+                                      cudaStream_t stream);
+/* tqkv_decode_int8_exchange with the fused append of tqkv_decode_int8_append
+ * (rows [S - T, S) of a cache of S_cap rows per head; T >= 1). */
+tqkv_status tqkv_decode_int8_append_exchange(const void* q,
+                                             const void* k_new, const void* v_new,
+                                             int8_t* kq, void* ks, int8_t* vq, void* vs,
+                                             void* o,
+                                             int B, int H, int T, int S, int S_cap, int D,
+                                             int block_size,
+                                             void* workspace, size_t workspace_bytes,
+                                             void* const* exchange_bufs, int world, int rank,
+                                             cudaStream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* INT8 decode for callers that cannot allocate device memory.
  * No counterpart in the reference.
@@ -288,10 +325,14 @@ tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o,
  *     stream capture;
  *   - all calls on a device share the one array: calls that can overlap on
  *     the GPU (different streams, or unordered host threads) race and must be
- *     ordered by the caller.
+ *     ordered by the caller;
+ *   - the array's address is looked up once per device and kept for the life
+ *     of the process: after cudaDeviceReset (which unloads the library's
+ *     device code) this entry point must not be called again.
  * Nothing is allocated: no cudaMalloc/cudaFree and no allocating library
- * routine; each call clears the array's ticket counters with a memset on
- * `stream` before launching. */
+ * routine; each call clears the part of the array its shape uses (counters
+ * and the records of split heads) with a memset on `stream` before
+ * launching. */
 #define TQKV_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
 
 tqkv_status tqkv_decode_int8_noalloc(const void* q,

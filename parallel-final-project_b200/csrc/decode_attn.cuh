@@ -17,10 +17,15 @@
 // CTAs claim from a counter in the workspace.  A chunk covers the tail of one
 // head, whole heads, and the head of another; each piece ("segment") yields an
 // online-softmax state (m, l, acc[D]).  A head that lies inside one chunk is
-// finished there; a head cut across chunks writes one partial per piece to
-// the workspace and the piece that arrives last (atomic ticket) merges them by
-// log-sum-exp and writes O.  Tickets, records and the claim counter are reset
-// by the kernel, so the workspace stays zeroed between calls.
+// finished there.  A head cut across chunks has every piece store its state
+// to the workspace as a record whose values carry a presence tag (no fence,
+// no atomic); the CTA that holds the head's first piece (the end of one of
+// its chunks) merges the head's records by log-sum-exp after it has streamed
+// all of its own chunks, and writes O.  Every CTA stores all of its records
+// before it waits for anyone else's, and the launch is cooperative (every CTA
+// resident), so the waits always end.  The merge zeroes the records it read
+// and the last producer resets the claim counter, so the workspace stays
+// zeroed between calls.
 //
 // CTA = 4 consumer warps + 1 producer warp.  One producer lane streams tiles
 // of TILE tokens (K rows, V rows, their fp16 scales, and q at the start of a
@@ -29,8 +34,9 @@
 // multicast), and describes each tile (head, offset, segment flags) in a
 // per-stage descriptor.  Consumers never touch global memory on the hot loop.
 //
-// Variants: OUT selects the epilogue (O, partial records, or records pushed
-// to every GPU's exchange buffer); APPEND (fused append) has the consumers
+// Variants: OUT selects the epilogue (O, partial records, records pushed to
+// every GPU's exchange buffer, or pushed and then merged into O by the same
+// launch); APPEND (fused append) has the consumers
 // quantise the newest rows of each head into the cache and the tile; group > 1
 // maps query head bh to K/V head bh / group (GQA/MQA).
 //
@@ -66,12 +72,18 @@ constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
 constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeTileBytes = 8192;  // bytes of K (and of V) per stage
 constexpr int kDecodeStages = 3;        // 3 stages x ~17.7 KB: four CTAs fit on an SM
+// Cut heads whose first piece one CTA holds, merged at its end: at most one
+// per chunk, so a CTA claims at most this many chunks (the plan hands out
+// far fewer per CTA on average).
+constexpr int kMaxDefer = 32;
 
 enum DecodeOut : int {
     kOutHalf = 0,     // write O (fp16)
     kOutPartial = 1,  // write per-head (acc[D], m, l) records, natural-log units
     kOutPeers = 2,    // write the records, tagged with the step number, into every
                       // rank's exchange buffer (split-S over NVLink)
+    kOutExchange = 3, // kOutPeers, then merge every rank's records into O in the
+                      // same launch (cooperative: see exchange_epilogue)
 };
 
 // Exchange buffer of one rank (split-S across the GPUs of a node), written by
@@ -107,6 +119,16 @@ __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned lon
 __device__ __forceinline__ unsigned long long pack_step(float v, unsigned int step) {
     return (static_cast<unsigned long long>(step) << 32) | __float_as_uint(v);
 }
+// Workspace records of cut heads' pieces: {float bits, 1}; zero = not stored.
+__device__ __forceinline__ unsigned long long tag_present(float v) {
+    return (1ull << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ bool is_present(unsigned long long w) {
+    return static_cast<unsigned int>(w >> 32) == 1u;
+}
+__device__ __forceinline__ float tagged_value(unsigned long long w) {
+    return __uint_as_float(static_cast<unsigned int>(w));
+}
 struct DecodeArgs {
     const void* q;             // fp16 [BH][D]
     const void* k;             // int8 or fp16 [BH][S][D]
@@ -114,8 +136,8 @@ struct DecodeArgs {
     const uint16_t* ks;        // fp16 [BH][S][D/BS] (INT8 only)
     const uint16_t* vs;
     void* out;                 // fp16 O [BH][D] or float [BH][D+2]
-    float* parts;              // workspace [BH][max_parts][D+4] (log2 units; see kRecFloats)
-    unsigned int* tickets;     // workspace [BH]
+    unsigned long long* recs;  // workspace [BH][max_parts][D+2]: tagged records of the pieces
+                               // of cut heads (acc[D], m in log2 units, l); zero between calls
     long long total_rows;      // BH * S
     long long chunk_rows;      // C: chunk u is rows [u * C, (u + 1) * C) of the BH * S rows
     unsigned int nchunks;      // ceil(total_rows / C)
@@ -126,10 +148,12 @@ struct DecodeArgs {
     int BH;
     int max_parts;
     float score_scale_log2;    // log2(e) / sqrt(D)
-    PeerArgs peer;             // kOutPeers only
+    PeerArgs peer;             // kOutPeers, kOutExchange
     const void* k_new;         // fused append only: fp16 [BH][T_new][D], rows [S - T_new, S)
     const void* v_new;
     int T_new;
+    unsigned int* fold;        // kOutExchange: workspace [0] heads claimed for merging,
+                               // [1] CTAs finished
 };
 
 template <int D, int BS, bool kHalfKV>
@@ -154,25 +178,26 @@ struct DecodeCfg {
     static constexpr int kStageBytes = kOffQ + kQSlot;
     // merge scratch after the ring
     static constexpr int kOffMerge = kDecodeStages * kStageBytes;
-    // Workspace record of a split head's piece: acc[D], m, l, 2 floats of
-    // padding, so that records start on 16 bytes and merge with float4 loads.
-    static constexpr int kRecFloats = D + 4;
-    // The merge of a split head splits the D dims into float4 groups over
-    // kRecLanes threads and the records into kRecSlices slices.
+    // Workspace record of a cut head's piece: D + 2 tagged 64-bit values
+    // (acc[D], m, l); 16-byte aligned, so the merge reads value pairs.
+    static constexpr int kRecWords = D + 2;
+    // The merge of a cut head gives each thread 4 dims (kRecLanes threads per
+    // record) and splits the records into kRecSlices slices.
     static constexpr int kRecLanes = D / 4;
     static constexpr int kRecSlices = kDecodeConsumers / kRecLanes;
-    // merge area: the warps' states; or, merging records, one weight per
-    // consumer thread / the slices' partial sums, then 8 reduction slots
+    // merge area: the warps' states ([warp][D + 2] floats), or the slices'
+    // states of a cut head's merge ([slice][D + 4]: rows start on 16 bytes)
+    static constexpr int kSliceStride = D + 4;
     static constexpr int kMergeFloats =
-        kDecodeConsumerWarps * (D + 2) > kRecSlices * D + 2 * kDecodeConsumerWarps
+        kDecodeConsumerWarps * (D + 2) > kRecSlices * kSliceStride
             ? kDecodeConsumerWarps * (D + 2)
-            : kRecSlices * D + 2 * kDecodeConsumerWarps;
-    static constexpr int kMergeBytes = kMergeFloats * 4;
-    static_assert(kRecSlices * D >= kDecodeConsumers, "weights fit under the slice sums");
+            : kRecSlices * kSliceStride;
+    static constexpr int kMergeBytes = (kMergeFloats * 4 + 15) / 16 * 16;
     static constexpr int kOffBars = kOffMerge + kMergeBytes;
     static constexpr int kOffMeta = kOffBars + 2 * kDecodeStages * 8;  // int[stages][8]
     static constexpr int kOffCtl = kOffMeta + kDecodeStages * 32;      // CtaCtl
-    static constexpr int kSmemBytes = kOffCtl + 32;
+    static constexpr int kOffDefer = kOffCtl + 32;                     // int2[kMaxDefer]
+    static constexpr int kSmemBytes = kOffDefer + kMaxDefer * 8;
 
     static_assert(kTPG == 4, "each lane group owns 4 rows per stage");
     static_assert(kStageBytes % 16 == 0, "stage must stay 16-byte aligned");
@@ -188,12 +213,15 @@ struct TileMeta {
     int pad;
 };
 
-// CTA control block in shared memory: the merge flag, and an abort flag that
-// a warp whose bounded wait ran out raises so that the others leave as well.
+// CTA control block in shared memory: the claim slot of the exchange
+// epilogue, an abort flag that a warp whose bounded wait ran out raises so
+// that the others leave as well, and the count of cut heads this CTA merges
+// at its end (listed after the block as (head, pieces) pairs).
 struct CtaCtl {
     int flag;
     unsigned int abort;
-    unsigned int pad[6];
+    int ndefer;
+    unsigned int pad[5];
 };
 static_assert(sizeof(CtaCtl) == 32, "CtaCtl layout");
 
@@ -357,9 +385,13 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     // head (and their indices) deterministic.  A chunk may cover the end of
     // one head and the start of the next: one segment per head.
     unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
+    int claimed = 0;
     while (ok) {
         unsigned int chunk;
         if (a.sched != nullptr) {
+            // each chunk may leave this CTA one cut head to merge at its end
+            if (claimed == kMaxDefer) break;
+            ++claimed;
             chunk = atomicAdd(&a.sched[0], 1u);
         } else {
             chunk = static_chunk;
@@ -783,6 +815,74 @@ __device__ __forceinline__ void lse_factors(float m, float mo, float& M, float& 
     fb = fast_exp2(mo - base);
 }
 
+// Merge the `world` records of head bh for `step` from this rank's exchange
+// buffer into O[bh][t] (one thread per dim t < D), natural-log units.  Every
+// load of the thread's 3 * world entries is issued at once (one round trip
+// when the peers are done, the usual case); only entries still carrying an
+// older step are polled again, for at most ~2^31 SM cycles (about a second).
+// On timeout the device error flag gets kErrPeerWaitTimeout and O[bh][t] is
+// NaN, so a lost peer shows in the output as well.
+template <int D>
+__device__ __forceinline__ void combine_head(const PeerArgs& p, int BH, int bh, int t,
+                                             unsigned int step, __half* __restrict__ o) {
+    const long long stride = static_cast<long long>(BH) * (D + 2);
+    const unsigned long long* rec =
+        p.own_recs + (static_cast<long long>(step & 1u) * p.world * BH + bh) * (D + 2);
+    unsigned long long v[3 * kMaxPeers];
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            v[3 * r] = ld_volatile_u64(rec + r * stride + D);
+            v[3 * r + 1] = ld_volatile_u64(rec + r * stride + D + 1);
+            v[3 * r + 2] = ld_volatile_u64(rec + r * stride + t);
+        }
+    }
+    bool ready = true;
+#pragma unroll
+    for (int i = 0; i < 3 * kMaxPeers; ++i)
+        if (i < 3 * p.world) ready = ready && static_cast<unsigned int>(v[i] >> 32) == step;
+    if (!ready) {
+        const long long start = clock64();
+#pragma unroll 1
+        for (uint32_t it = 0; it < (1u << 30) && !ready; ++it) {
+            ready = true;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r < p.world) {
+                    const unsigned long long* base = rec + r * stride;
+                    if (static_cast<unsigned int>(v[3 * r] >> 32) != step) v[3 * r] = ld_volatile_u64(base + D);
+                    if (static_cast<unsigned int>(v[3 * r + 1] >> 32) != step) v[3 * r + 1] = ld_volatile_u64(base + D + 1);
+                    if (static_cast<unsigned int>(v[3 * r + 2] >> 32) != step) v[3 * r + 2] = ld_volatile_u64(base + t);
+                    ready = ready && static_cast<unsigned int>(v[3 * r] >> 32) == step &&
+                            static_cast<unsigned int>(v[3 * r + 1] >> 32) == step &&
+                            static_cast<unsigned int>(v[3 * r + 2] >> 32) == step;
+                }
+            }
+            if (clock64() - start > (1ll << 31)) break;
+        }
+        if (!ready) {
+            record_device_error(kErrPeerWaitTimeout);
+            o[static_cast<long long>(bh) * D + t] = __ushort_as_half(static_cast<unsigned short>(0x7e00u));
+            return;
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+        if (r < p.world) M = fmaxf(M, __uint_as_float(static_cast<unsigned int>(v[3 * r])));
+    const float base = M == -INFINITY ? 0.0f : M;
+    float A = 0.0f, L = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            const float f = __expf(__uint_as_float(static_cast<unsigned int>(v[3 * r])) - base);
+            L = fmaf(__uint_as_float(static_cast<unsigned int>(v[3 * r + 1])), f, L);
+            A = fmaf(__uint_as_float(static_cast<unsigned int>(v[3 * r + 2])), f, A);
+        }
+    }
+    o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
+}
+
 // Write a finished head: O (fp16), a partial record, or the record in every
 // rank's exchange buffer followed, for the step's last head, by the step flag.
 // All consumer threads call it; A is this thread's dim (tid < D); M2 is in
@@ -831,9 +931,10 @@ __device__ __forceinline__ void emit_head(const DecodeArgs& a, int bh, int tid, 
 }
 
 // Finish one segment: merge the lane-group states of the CTA, then either
-// write O / the partial record (head held by one chunk), or publish a partial
-// and let the last chunk of the head to finish merge all of them.  Returns
-// false when a consumer barrier gave up (the CTA then leaves).
+// write O / the partial record (head held by one chunk), or store the piece's
+// tagged record for the head's merge (merge_cut_head, run at the end of the
+// CTA that holds part 0, which this call lists when it is that part).
+// Returns false when a consumer barrier gave up (the CTA then leaves).
 template <int D, int BS, bool kHalfKV, int OUT>
 __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, const DecodeArgs& a,
                                                float* merge, CtaCtl* ctl, int bh, int part,
@@ -901,96 +1002,161 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
         return consumer_barrier(ctl);  // merge[] is reused by the next segment
     }
 
-    // publish this CTA's piece of the head
-    float* mine = a.parts + (static_cast<long long>(bh) * a.max_parts + part) * C::kRecFloats;
-    if (tid < D) {
-        mine[tid] = A;
-        if (tid == 0) {
-            mine[D] = M;
-            mine[D + 1] = L;
+    // A piece of a head cut across chunks: store its record, every value
+    // tagged as present, and go on streaming.  The CTA holding the head's
+    // first piece merges all of them once it has streamed all of its chunks.
+    unsigned long long* rec =
+        a.recs + (static_cast<long long>(bh) * a.max_parts + part) * C::kRecWords;
+    if (tid < D) st_relaxed_u64(rec + tid, tag_present(A));
+    if (tid == 0) {
+        st_relaxed_u64(rec + D, tag_present(M));
+        st_relaxed_u64(rec + D + 1, tag_present(L));
+        if (part == 0) {
+            int2* defer = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(ctl) + 32);
+            const int n = ctl->ndefer;
+            if (n < kMaxDefer) {
+                defer[n] = make_int2(bh, nparts);
+                ctl->ndefer = n + 1;
+            } else {
+                record_device_error(kErrDeferOverflow);
+            }
         }
     }
-    // every thread's record stores happen before thread 0's fence through the
-    // barrier, and the fence (cumulative) orders them before the ticket
+    // merge[] (and the list) are reused by the next segment
+    return consumer_barrier(ctl);
+}
+
+// Merge the `nparts` records of cut head bh (log-sum-exp, in part order, so
+// the result does not depend on which CTA streamed which piece) and emit the
+// head.  Threads take 4 dims each (kRecLanes per record) and one slice of the
+// records (parts sl, sl + kRecSlices, ...), loading 4 parts at a time and
+// polling, bounded (~2^31 SM cycles), only values whose tag is not yet set;
+// the slices' states are then merged through shared memory.  The records are
+// zeroed afterwards.  On timeout: kErrPieceWaitTimeout, the head is emitted
+// from the pieces that did arrive.  Returns false when a consumer barrier
+// gave up.
+template <int D, int BS, bool kHalfKV, int OUT>
+__device__ __forceinline__ bool merge_cut_head(const DecodeArgs& a, float* merge, CtaCtl* ctl, int bh,
+                                            int nparts, int tid) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    constexpr int kBatch = 4;
+    const int dq = tid % C::kRecLanes;   // dims 4*dq .. 4*dq + 3
+    const int sl = tid / C::kRecLanes;   // records sl, sl + kRecSlices, ...
+    const unsigned long long* recs =
+        a.recs + static_cast<long long>(bh) * a.max_parts * C::kRecWords;
+    float M = -INFINITY, L = 0.0f;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const long long start = clock64();
+    bool late = false;
+#pragma unroll 1
+    for (int p0 = sl; p0 < nparts; p0 += kBatch * C::kRecSlices) {
+        ulonglong2 ml[kBatch], a01[kBatch], a23[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int p = p0 + j * C::kRecSlices;
+            if (p < nparts) {
+                const unsigned long long* r = recs + p * C::kRecWords;
+                ml[j] = ld_relaxed_u64x2(r + D);
+                a01[j] = ld_relaxed_u64x2(r + 4 * dq);
+                a23[j] = ld_relaxed_u64x2(r + 4 * dq + 2);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int p = p0 + j * C::kRecSlices;
+            if (p >= nparts) continue;
+            const unsigned long long* r = recs + p * C::kRecWords;
+            // poll only what has not arrived yet
+#pragma unroll 1
+            while (!(is_present(ml[j].x) && is_present(ml[j].y) && is_present(a01[j].x) &&
+                     is_present(a01[j].y) && is_present(a23[j].x) && is_present(a23[j].y))) {
+                if (late || clock64() - start > (1ll << 31)) {
+                    late = true;
+                    break;
+                }
+                if (!(is_present(ml[j].x) && is_present(ml[j].y))) ml[j] = ld_relaxed_u64x2(r + D);
+                if (!(is_present(a01[j].x) && is_present(a01[j].y))) a01[j] = ld_relaxed_u64x2(r + 4 * dq);
+                if (!(is_present(a23[j].x) && is_present(a23[j].y)))
+                    a23[j] = ld_relaxed_u64x2(r + 4 * dq + 2);
+            }
+            if (late && !(is_present(ml[j].x) && is_present(ml[j].y))) continue;
+            const float m = tagged_value(ml[j].x), l = tagged_value(ml[j].y);
+            if (m > M) {
+                const float s = fast_exp2(M - m);  // 2^-inf = 0 for the first piece
+                L *= s;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i] *= s;
+                M = m;
+            }
+            const float f = fast_exp2(m - M);
+            L = fmaf(l, f, L);
+            acc[0] = fmaf(tagged_value(a01[j].x), f, acc[0]);
+            acc[1] = fmaf(tagged_value(a01[j].y), f, acc[1]);
+            acc[2] = fmaf(tagged_value(a23[j].x), f, acc[2]);
+            acc[3] = fmaf(tagged_value(a23[j].y), f, acc[3]);
+        }
+    }
+    if (late) record_device_error(kErrPieceWaitTimeout);
+    // the slices' states: merge[sl][0..D-1] = acc, [D] = M, [D+1] = L
+    float* ms = merge + sl * C::kSliceStride;
+    *reinterpret_cast<float4*>(ms + 4 * dq) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (dq == 0) {
+        ms[D] = M;
+        ms[D + 1] = L;
+    }
     if (!consumer_barrier(ctl)) return false;
+    float At = 0.0f, Mt = -INFINITY, Lt = 0.0f;
+    if (tid < D) {
+#pragma unroll
+        for (int k = 0; k < C::kRecSlices; ++k) Mt = fmaxf(Mt, merge[k * C::kSliceStride + D]);
+        const float base = Mt == -INFINITY ? 0.0f : Mt;
+#pragma unroll
+        for (int k = 0; k < C::kRecSlices; ++k) {
+            const float f = fast_exp2(merge[k * C::kSliceStride + D] - base);
+            Lt = fmaf(merge[k * C::kSliceStride + D + 1], f, Lt);
+            At = fmaf(merge[k * C::kSliceStride + tid], f, At);
+        }
+    }
+    emit_head<D, OUT>(a, bh, tid, At, Mt, Lt);
+    // leave the workspace all-zero for the next call, whatever its shape
+    unsigned long long* z =
+        a.recs + static_cast<long long>(bh) * a.max_parts * C::kRecWords;
+    for (int i = tid; i < nparts * C::kRecWords; i += kDecodeConsumers) z[i] = 0ull;
+    return consumer_barrier(ctl);  // merge[] is reused by the next merge
+}
+
+// kOutExchange, after a CTA's last segment: the CTA claims heads from a
+// counter and merges every rank's records of each into O (combine_head), then
+// counts itself out; the last CTA of the launch resets the counters and
+// advances this rank's step.  A claimed head's records come from every rank,
+// this one included, i.e. from other CTAs of this launch, so the launch must
+// be cooperative (every CTA resident; the plan's grid never exceeds the
+// resident CTAs).  Across ranks nothing is circular: each rank emits all of
+// its records of the step before any of its CTAs waits.  Returns false when a
+// consumer barrier gave up.
+template <int D>
+__device__ __forceinline__ bool exchange_epilogue(const DecodeArgs& a, CtaCtl* ctl, int tid) {
+    const unsigned int step = __ldcg(a.peer.own + kHdrEpoch) + 1u;
+    __half* o = static_cast<__half*>(a.out);
+    for (;;) {
+        if (tid == 0) ctl->flag = static_cast<int>(atomicAdd(&a.fold[0], 1u));
+        if (!consumer_barrier(ctl)) return false;
+        const int h = *reinterpret_cast<volatile int*>(&ctl->flag);
+        // every thread has read the claim before thread 0 writes the next one
+        if (!consumer_barrier(ctl)) return false;
+        if (h < 0 || h >= a.BH) break;
+        if (tid < D) combine_head<D>(a.peer, a.BH, h, tid, step, o);
+    }
     if (tid == 0) {
         __threadfence();
-        const unsigned int prev = atomicAdd(&a.tickets[bh], 1u);
-        ctl->flag = (prev == static_cast<unsigned int>(nparts - 1)) ? 1 : 0;
-    }
-    if (!consumer_barrier(ctl)) return false;
-    // Not the last piece: done.  Every read of merge[] happened before the
-    // barrier after the record stores, so the next segment may overwrite it.
-    if (!*reinterpret_cast<volatile int*>(&ctl->flag)) return true;
-    {
-        // Last piece of the head: merge its nparts records.  The records are
-        // spread over the consumer threads (one per thread for the maxima and
-        // weights; float4 groups of dims x record slices for acc) so the L2
-        // reads overlap instead of running one by one.
-        __threadfence();
-        constexpr int kRec = C::kRecFloats;
-        const float* recs = a.parts + static_cast<long long>(bh) * a.max_parts * kRec;
-        float* fw = merge;                                  // weights of one batch of records
-        float* red = merge + C::kRecSlices * D;             // [0..3] warp maxima, [4..7] sums
-        float mloc = -INFINITY;
-        for (int p = tid; p < nparts; p += kDecodeConsumers)
-            mloc = fmaxf(mloc, __ldcg(recs + p * kRec + D));
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-            mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
-        if (lane == 0) red[warp] = mloc;
-        if (!consumer_barrier(ctl)) return false;
-        float Mt = red[0];
-#pragma unroll
-        for (int w = 1; w < kDecodeConsumerWarps; ++w) Mt = fmaxf(Mt, red[w]);
-        const float base = Mt == -INFINITY ? 0.0f : Mt;
-        const int dq = tid % C::kRecLanes;   // dims 4*dq .. 4*dq + 3
-        const int sl = tid / C::kRecLanes;   // records sl, sl + kRecSlices, ...
-        float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        float Lloc = 0.0f;
-        for (int b0 = 0; b0 < nparts; b0 += kDecodeConsumers) {
-            const int nb = (nparts - b0) < kDecodeConsumers ? (nparts - b0) : kDecodeConsumers;
-            if (tid < nb) {
-                const float* rp = recs + (b0 + tid) * kRec;
-                const float f = fast_exp2(__ldcg(rp + D) - base);
-                fw[tid] = f;
-                Lloc = fmaf(__ldcg(rp + D + 1), f, Lloc);
-            }
-            if (!consumer_barrier(ctl)) return false;
-            const float4* rp = reinterpret_cast<const float4*>(recs + b0 * kRec) + dq;
-#pragma unroll 4
-            for (int k = sl; k < nb; k += C::kRecSlices) {
-                const float4 r = __ldcg(rp + k * (kRec / 4));
-                const float f = fw[k];
-                acc4.x = fmaf(r.x, f, acc4.x);
-                acc4.y = fmaf(r.y, f, acc4.y);
-                acc4.z = fmaf(r.z, f, acc4.z);
-                acc4.w = fmaf(r.w, f, acc4.w);
-            }
-            if (b0 + kDecodeConsumers < nparts && !consumer_barrier(ctl)) return false;
+        if (atomicAdd(&a.fold[1], 1u) == gridDim.x - 1) {
+            // every CTA has emitted, claimed and merged: the step is done here
+            atomicExch(&a.fold[0], 0u);
+            atomicExch(&a.fold[1], 0u);
+            a.peer.own[kHdrEpoch] = step;
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) Lloc += __shfl_xor_sync(0xffffffffu, Lloc, off);
-        if (lane == 0) red[kDecodeConsumerWarps + warp] = Lloc;
-        // every record (and weight) has been read once all warps pass this barrier
-        if (!consumer_barrier(ctl)) return false;
-        *reinterpret_cast<float4*>(merge + sl * D + 4 * dq) = acc4;
-        if (!consumer_barrier(ctl)) return false;
-        float At = 0.0f, Lt = 0.0f;
-        if (tid < D) {
-#pragma unroll
-            for (int k = 0; k < C::kRecSlices; ++k) At += merge[k * D + tid];
-        }
-#pragma unroll
-        for (int w = 0; w < kDecodeConsumerWarps; ++w) Lt += red[kDecodeConsumerWarps + w];
-        emit_head<D, OUT>(a, bh, tid, At, Mt, Lt);
-        // leave the workspace all-zero for the next call, whatever its shape:
-        // the ticket, and every record this merge consumed
-        float* zrec = a.parts + static_cast<long long>(bh) * a.max_parts * kRec;
-        for (int i = tid; i < nparts * kRec; i += kDecodeConsumers) zrec[i] = 0.0f;
-        if (tid == 0) a.tickets[bh] = 0u;
     }
-    return consumer_barrier(ctl);
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -1014,6 +1180,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         }
         ctl->flag = 0;
         ctl->abort = 0u;
+        ctl->ndefer = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -1042,7 +1209,23 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
             return;
         }
         const TileMeta m = meta[stage];
-        if (m.flags & kTileDone) return;
+        if (m.flags & kTileDone) {
+            // the cut heads whose first piece this CTA streamed (list written
+            // by thread 0 before the last segment's closing barrier)
+            const int nd = *reinterpret_cast<volatile int*>(&ctl->ndefer);
+            const int2* defer = reinterpret_cast<const int2*>(reinterpret_cast<uint8_t*>(ctl) + 32);
+            for (int i = 0; i < nd; ++i) {
+                const int2 e = defer[i];
+                if (!merge_cut_head<D, BS, kHalfKV, OUT>(a, merge, ctl, e.x, e.y, tid)) {
+                    consumer_leave(ctl);
+                    return;
+                }
+            }
+            if constexpr (OUT == kOutExchange) {
+                if (!exchange_epilogue<D>(a, ctl, tid)) consumer_leave(ctl);
+            }
+            return;
+        }
         const uint8_t* sp = smem + stage * C::kStageBytes;
         if (m.flags & kTileFirst) {
             const int q_off = static_cast<int>(
@@ -1104,77 +1287,17 @@ __global__ void __launch_bounds__(D)
     o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
 }
 
-// Split-S step over NVLink, second half: wait (bounded) until every rank has
-// published the current step into this rank's exchange buffer, then merge the
-// world records of each head (natural-log units) into O.  One CTA per head.
+// Split-S step over NVLink, second half (two-launch form): wait (bounded)
+// until every rank has published the current step into this rank's exchange
+// buffer, then merge the world records of each head into O.  One CTA per
+// head; the last CTA advances this rank's step counter.
 template <int D>
 __global__ void __launch_bounds__(D)
     exchange_combine_kernel(const PeerArgs p, __half* __restrict__ o, int BH) {
     const int bh = blockIdx.x;
     const int t = threadIdx.x;
     const unsigned int step = __ldcg(p.own + kHdrEpoch) + 1u;
-    const long long stride = static_cast<long long>(BH) * (D + 2);
-    const unsigned long long* rec =
-        p.own_recs + (static_cast<long long>(step & 1u) * p.world * BH + bh) * (D + 2);
-    // Issue every load of this thread's 3 * world entries at once (one round
-    // trip when the peers are done, the usual case), then re-poll only while
-    // some entry still carries an older step.
-    unsigned long long v[3 * kMaxPeers];
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r) {
-        if (r < p.world) {
-            v[3 * r] = ld_volatile_u64(rec + r * stride + D);
-            v[3 * r + 1] = ld_volatile_u64(rec + r * stride + D + 1);
-            v[3 * r + 2] = ld_volatile_u64(rec + r * stride + t);
-        }
-    }
-    bool ready = true;
-#pragma unroll
-    for (int i = 0; i < 3 * kMaxPeers; ++i)
-        if (i < 3 * p.world) ready = ready && static_cast<unsigned int>(v[i] >> 32) == step;
-    if (!ready) {
-        const long long start = clock64();
-#pragma unroll 1
-        for (uint32_t it = 0; it < (1u << 30) && !ready; ++it) {
-            ready = true;
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r < p.world) {
-                    const unsigned long long* base = rec + r * stride;
-                    if (static_cast<unsigned int>(v[3 * r] >> 32) != step) v[3 * r] = ld_volatile_u64(base + D);
-                    if (static_cast<unsigned int>(v[3 * r + 1] >> 32) != step) v[3 * r + 1] = ld_volatile_u64(base + D + 1);
-                    if (static_cast<unsigned int>(v[3 * r + 2] >> 32) != step) v[3 * r + 2] = ld_volatile_u64(base + t);
-                    ready = ready && static_cast<unsigned int>(v[3 * r] >> 32) == step &&
-                            static_cast<unsigned int>(v[3 * r + 1] >> 32) == step &&
-                            static_cast<unsigned int>(v[3 * r + 2] >> 32) == step;
-                }
-            }
-            if (clock64() - start > (1ll << 31)) break;
-        }
-        if (!ready) record_device_error(kErrPeerWaitTimeout);
-    }
-    float m[kMaxPeers], l[kMaxPeers], acc[kMaxPeers];
-    float M = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r) {
-        if (r < p.world) {
-            m[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r]));
-            l[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r + 1]));
-            acc[r] = __uint_as_float(static_cast<unsigned int>(v[3 * r + 2]));
-            M = fmaxf(M, m[r]);
-        }
-    }
-    const float base = M == -INFINITY ? 0.0f : M;
-    float A = 0.0f, L = 0.0f;
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r) {
-        if (r < p.world) {
-            const float f = __expf(m[r] - base);
-            L = fmaf(l[r], f, L);
-            A = fmaf(acc[r], f, A);
-        }
-    }
-    o[static_cast<long long>(bh) * D + t] = __float2half_rn(A * (1.0f / L));
+    combine_head<D>(p, BH, bh, t, step, o);
     // the last CTA of the step advances this rank's step counter; every CTA
     // has read it above, before adding itself to the count
     __syncthreads();
@@ -1184,6 +1307,28 @@ __global__ void __launch_bounds__(D)
         if (prev == static_cast<unsigned int>(BH - 1)) {
             p.own[kHdrDone] = 0u;
             p.own[kHdrEpoch] = step;
+        }
+    }
+}
+
+// Empty records (acc = 0, m = -inf, l = 0) of the current step into every
+// rank's exchange buffer, for a rank whose token slice is empty (S == 0).
+// One CTA per head, one thread per dim.
+template <int D>
+__global__ void __launch_bounds__(D) publish_empty_kernel(const PeerArgs p, int BH) {
+    const int bh = blockIdx.x;
+    const int t = threadIdx.x;
+    const unsigned int step = __ldcg(p.own + kHdrEpoch) + 1u;
+    const long long off =
+        ((static_cast<long long>(step & 1u) * p.world + p.rank) * BH + bh) * (D + 2);
+    for (int r = 0; r < kMaxPeers; ++r) {
+        if (r < p.world) {
+            unsigned long long* rec = p.recs[r] + off;
+            st_volatile_u64(rec + t, pack_step(0.0f, step));
+            if (t == 0) {
+                st_volatile_u64(rec + D, pack_step(-INFINITY, step));
+                st_volatile_u64(rec + D + 1, pack_step(0.0f, step));
+            }
         }
     }
 }

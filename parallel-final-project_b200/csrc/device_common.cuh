@@ -21,6 +21,9 @@ enum DeviceErrorCode : unsigned int {
     kErrEmptyWaitTimeout = 2,    // producer waited too long for a free stage
     kErrDrainTimeout = 3,        // producer's copies never completed
     kErrPeerWaitTimeout = 4,     // a peer GPU's exchange entries never arrived
+    kErrPieceWaitTimeout = 5,    // a piece of a head split across CTAs never arrived
+    kErrDeferOverflow = 6,       // more first pieces than a CTA can hold (cannot happen:
+                                 // the producer stops claiming chunks before that)
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {
@@ -76,6 +79,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         if (clock64() - start > (1ll << 31)) break;
     }
     return false;
+}
+
+// Relaxed 64-bit global accesses at GPU scope (one CTA's stores, another
+// CTA's loads; every value carries its own presence tag, so no fences).
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_relaxed_u64x2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];"
+                 : "=l"(v.x), "=l"(v.y)
+                 : "l"(p)
+                 : "memory");
+    return v;
 }
 
 // L2 policy for data that is read exactly once per step (the KV stream).

@@ -42,6 +42,9 @@ thread_local int t_last_cuda_error = 0;
 
 constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipeline fill
 constexpr long long kChunksPerCta = 8;     // scheduling chunks per CTA (load balance)
+// A CTA claims at most kMaxDefer chunks; the plan's kChunksPerCta per CTA on
+// average leaves room for CTAs that stream four times faster than the rest.
+static_assert(4 * kChunksPerCta <= kMaxDefer, "chunk claims per CTA");
 constexpr long long kChunkAlign = 128;     // chunk rows: a multiple of every tile height
 // Below this many rows per CTA every CTA takes one run of rows, statically:
 // each chunk boundary costs a head piece (a record, a ticket and consumer
@@ -144,19 +147,20 @@ DecodePlan bound_plan(long long BH, int S, int device) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// [0, 16): chunk scheduler counters; [16, ...): one ticket per head; then,
-// 256-aligned, max_parts partial records per head.  All zero between calls.
+// [0, 16): counters (chunk scheduler: next chunk, producers done; exchange
+// epilogue: heads claimed, CTAs done); from 256: max_parts tagged records of
+// D + 2 64-bit values per head.  All zero between calls.
 struct WsLayout {
-    size_t sched_off, tickets_off, parts_off, total;
+    size_t sched_off, parts_off, total;
 };
 
 WsLayout ws_layout(long long BH, int max_parts, int D) {
     WsLayout w{};
     w.sched_off = 0;
-    w.tickets_off = 16;
-    w.parts_off = decode_ws_counter_bytes(BH);
+    w.parts_off = 256;
     w.total = w.parts_off +
-              align_up(static_cast<size_t>(BH) * max_parts * (D + 4) * sizeof(float), 256);
+              align_up(static_cast<size_t>(BH) * max_parts * (D + 2) * sizeof(unsigned long long),
+                       256);
     return w;
 }
 
@@ -177,6 +181,31 @@ cudaError_t launch_kernel(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t sm
         ((ptrs[i++] = static_cast<void*>(&v)), ...);
     }, vals);
     return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, block, ptrs, smem, stream);
+}
+
+// Cooperative launch (every CTA of the grid resident at once), for kernels
+// whose CTAs wait on one another.  Same error behaviour as launch_kernel.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_coop(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, Args... args) {
+    static_assert(sizeof...(KArgs) == sizeof...(Args), "argument count");
+    std::tuple<KArgs...> vals(static_cast<KArgs>(args)...);
+    void* ptrs[sizeof...(KArgs) > 0 ? sizeof...(KArgs) : 1];
+    std::apply([&](auto&... v) {
+        int i = 0;
+        ((ptrs[i++] = static_cast<void*>(&v)), ...);
+    }, vals);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(fn), ptrs);
 }
 
 template <int D, int BS>
@@ -240,16 +269,17 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     const long long resident = static_cast<long long>(sm_count(dev)) * occ;
     const DecodePlan plan = make_plan(BH, S, resident);
     if (plan.max_parts > bound.max_parts) return TQKV_ERR_WORKSPACE;  // cannot happen: occ <= bound
-    // records and tickets for cut heads; the claim counter for dynamic chunks
-    const bool needs_ws = plan.nchunks > 1;
+    // records and tickets for cut heads; the claim counter for dynamic chunks;
+    // the merge counters of the one-launch exchange
+    constexpr bool kFold = OUT == kOutExchange;
+    const bool needs_ws = plan.nchunks > 1 || kFold;
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     // one chunk per CTA: no claims, chunk = blockIdx.x
     a.sched = plan.nchunks > plan.grid ? reinterpret_cast<unsigned int*>(ws + lay.sched_off)
                                         : nullptr;
-    a.tickets = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.tickets_off) : nullptr;
-    a.parts = needs_ws ? reinterpret_cast<float*>(ws + lay.parts_off) : nullptr;
+    a.recs = needs_ws ? reinterpret_cast<unsigned long long*>(ws + lay.parts_off) : nullptr;
     a.total_rows = static_cast<long long>(BH) * S;
     a.chunk_rows = plan.chunk_rows;
     a.nchunks = static_cast<unsigned int>(plan.nchunks);
@@ -257,8 +287,13 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     a.BH = BH;
     a.max_parts = bound.max_parts;
     a.score_scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
-    return from_cuda(launch_kernel(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
-                                   stream, a));
+    // counters [2], [3] of the scheduler area
+    if constexpr (kFold) a.fold = reinterpret_cast<unsigned int*>(ws + lay.sched_off) + 2;
+    // Cooperative: a CTA may wait for the records of pieces that other CTAs
+    // stream (and, exchanging, merge), so every CTA must be resident; the
+    // plan's grid never exceeds the resident CTAs.
+    return from_cuda(launch_kernel_coop(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
+                                        stream, a));
 }
 
 template <int D, int BS, bool kHalfKV>
@@ -271,29 +306,36 @@ tqkv_status decode_out(OutKind out, const DecodeArgs& a, long long total, int S,
             return decode_impl<D, BS, false, kOutHalf, kAppend>(a, total, S, BH, ws, wsb, stream);
         if (a.T_new > 0 && out == OutKind::kPeers)
             return decode_impl<D, BS, false, kOutPeers, kAppend>(a, total, S, BH, ws, wsb, stream);
+        if (a.T_new > 0 && out == OutKind::kExchange)
+            return decode_impl<D, BS, false, kOutExchange, kAppend>(a, total, S, BH, ws, wsb, stream);
     }
     if (a.T_new > 0) return TQKV_ERR_UNSUPPORTED;
     if (out == OutKind::kHalfO)
         return decode_impl<D, BS, kHalfKV, kOutHalf>(a, total, S, BH, ws, wsb, stream);
     if (out == OutKind::kPartial)
         return decode_impl<D, BS, kHalfKV, kOutPartial>(a, total, S, BH, ws, wsb, stream);
-    if constexpr (!kHalfKV)
+    if constexpr (!kHalfKV) {
+        if (out == OutKind::kExchange)
+            return decode_impl<D, BS, kHalfKV, kOutExchange>(a, total, S, BH, ws, wsb, stream);
         return decode_impl<D, BS, kHalfKV, kOutPeers>(a, total, S, BH, ws, wsb, stream);
+    }
     return TQKV_ERR_UNSUPPORTED;
 }
 
-// INT8 decode with the kOutPeers epilogue (split-S over NVLink).
-tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void* k, const void* ks,
-                                const void* v, const void* vs, int BH, int S, int D, int bs,
-                                void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                                int S_stride = 0, const AppendRows* append = nullptr) {
+// INT8 decode with the kOutPeers epilogue (split-S over NVLink), or with
+// kOutExchange (the same, then the merge into O in the same launch).
+tqkv_status launch_decode_peers(OutKind o_kind, const PeerArgs& peer, const void* q, const void* k,
+                                const void* ks, const void* v, const void* vs, void* o, int BH,
+                                int S, int D, int bs, void* workspace, size_t workspace_bytes,
+                                cudaStream_t stream, int S_stride = 0,
+                                const AppendRows* append = nullptr) {
     DecodeArgs a{};
     a.q = q;
     a.k = k;
     a.v = v;
     a.ks = static_cast<const uint16_t*>(ks);
     a.vs = static_cast<const uint16_t*>(vs);
-    a.out = nullptr;
+    a.out = o_kind == OutKind::kExchange ? o : nullptr;
     a.peer = peer;
     a.S_stride = S_stride > 0 ? S_stride : S;
     a.group = 1;
@@ -303,12 +345,12 @@ tqkv_status launch_decode_peers(const PeerArgs& peer, const void* q, const void*
         a.T_new = append->T;
     }
     const long long total = static_cast<long long>(BH) * S;
-    const OutKind o = OutKind::kPeers;
-    if (D == 64 && bs == 32) return decode_out<64, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
-    if (D == 64 && bs == 64) return decode_out<64, 64, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
-    if (D == 128 && bs == 32) return decode_out<128, 32, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
-    if (D == 128 && bs == 64) return decode_out<128, 64, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
-    if (D == 128 && bs == 128) return decode_out<128, 128, false>(o, a, total, S, BH, workspace, workspace_bytes, stream);
+    const OutKind kind = o_kind;
+    if (D == 64 && bs == 32) return decode_out<64, 32, false>(kind, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 64 && bs == 64) return decode_out<64, 64, false>(kind, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 32) return decode_out<128, 32, false>(kind, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 64) return decode_out<128, 64, false>(kind, a, total, S, BH, workspace, workspace_bytes, stream);
+    if (D == 128 && bs == 128) return decode_out<128, 128, false>(kind, a, total, S, BH, workspace, workspace_bytes, stream);
     return TQKV_ERR_UNSUPPORTED;
 }
 
@@ -332,6 +374,22 @@ tqkv_status make_peer_args(void* const* bufs, int world, int rank, PeerArgs* out
     peer.rank = rank;
     *out = peer;
     return TQKV_OK;
+}
+
+// The two small launches of a step for a rank whose token slice is empty:
+// empty records into every rank's buffer; with `o`, then the merge into O.
+tqkv_status publish_empty(const PeerArgs& peer, void* o, int BH, int D, cudaStream_t stream) {
+    cudaError_t e;
+    if (D == 64)
+        e = launch_kernel(publish_empty_kernel<64>, dim3(BH), dim3(64), 0, stream, peer, BH);
+    else
+        e = launch_kernel(publish_empty_kernel<128>, dim3(BH), dim3(128), 0, stream, peer, BH);
+    if (e != cudaSuccess || o == nullptr) return from_cuda(e);
+    if (D == 64)
+        return from_cuda(launch_kernel(exchange_combine_kernel<64>, dim3(BH), dim3(64), 0, stream,
+                                       peer, static_cast<__half*>(o), BH));
+    return from_cuda(launch_kernel(exchange_combine_kernel<128>, dim3(BH), dim3(128), 0, stream,
+                                   peer, static_cast<__half*>(o), BH));
 }
 
 template <int D>
@@ -430,10 +488,6 @@ tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t
     if (grid > 1024) grid = 1024;
     return from_cuda(launch_kernel(fill_empty_partials_kernel, dim3(static_cast<unsigned>(grid)),
                                    dim3(256), 0, stream, p, heads, D));
-}
-
-size_t decode_ws_counter_bytes(long long BH) {
-    return align_up(16 + static_cast<size_t>(BH) * sizeof(unsigned int), 256);
 }
 
 size_t decode_workspace_bytes(long long BH, int S, int D) {
@@ -742,37 +796,44 @@ tqkv_status tqkv_ipc_close_handle(void* buf) {
     return tqkv::from_cuda(cudaIpcCloseMemHandle(buf));
 }
 
-tqkv_status tqkv_decode_int8_publish(const void* q, const int8_t* kq, const void* ks,
-                                     const int8_t* vq, const void* vs, int B, int H, int S, int D,
-                                     int block_size, void* workspace, size_t workspace_bytes,
-                                     void* const* exchange_bufs, int world, int rank,
-                                     cudaStream_t stream) {
+namespace {
+// Shared by the publish (two-launch) and exchange (one-launch) entry points.
+tqkv_status decode_split_step(OutKind kind, const void* q, const int8_t* kq, const void* ks,
+                              const int8_t* vq, const void* vs, void* o, int B, int H, int S,
+                              int D, int block_size, void* workspace, size_t workspace_bytes,
+                              void* const* exchange_bufs, int world, int rank,
+                              cudaStream_t stream) {
     if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
-    if (B <= 0 || H <= 0 || S <= 0 || world <= 0 || world > tqkv::kMaxPeers || rank < 0 ||
+    if (B <= 0 || H <= 0 || S < 0 || world <= 0 || world > tqkv::kMaxPeers || rank < 0 ||
         rank >= world)
         return TQKV_ERR_INVALID_SIZE;
-    if (!q || !kq || !ks || !vq || !vs || !exchange_bufs) return TQKV_ERR_NULL;
-    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    if (!q || !exchange_bufs || (kind == OutKind::kExchange && !o)) return TQKV_ERR_NULL;
     const long long BH = static_cast<long long>(B) * H;
     if (BH > 0x7fffffffLL) return TQKV_ERR_INVALID_SIZE;
     tqkv::PeerArgs peer{};
     const tqkv_status pst = tqkv::make_peer_args(exchange_bufs, world, rank, &peer);
     if (pst != TQKV_OK) return pst;
-    return tqkv::launch_decode_peers(peer, q, kq, ks, vq, vs, static_cast<int>(BH), S, D,
+    if (S == 0)
+        return tqkv::publish_empty(peer, kind == OutKind::kExchange ? o : nullptr,
+                                   static_cast<int>(BH), D, stream);
+    if (!kq || !ks || !vq || !vs) return TQKV_ERR_NULL;
+    if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq)) return TQKV_ERR_MISALIGNED;
+    return tqkv::launch_decode_peers(kind, peer, q, kq, ks, vq, vs, o, static_cast<int>(BH), S, D,
                                      block_size, workspace, workspace_bytes, stream);
 }
 
-tqkv_status tqkv_decode_int8_append_publish(const void* q, const void* k_new, const void* v_new,
-                                            int8_t* kq, void* ks, int8_t* vq, void* vs, int B,
-                                            int H, int T, int S, int S_cap, int D, int block_size,
-                                            void* workspace, size_t workspace_bytes,
-                                            void* const* exchange_bufs, int world, int rank,
-                                            cudaStream_t stream) {
+tqkv_status decode_split_step_append(OutKind kind, const void* q, const void* k_new,
+                                     const void* v_new, int8_t* kq, void* ks, int8_t* vq,
+                                     void* vs, void* o, int B, int H, int T, int S, int S_cap,
+                                     int D, int block_size, void* workspace,
+                                     size_t workspace_bytes, void* const* exchange_bufs,
+                                     int world, int rank, cudaStream_t stream) {
     if (!tqkv::is_supported_int8(D, block_size)) return TQKV_ERR_UNSUPPORTED;
     if (B <= 0 || H <= 0 || T <= 0 || S < T || S_cap < S || world <= 0 ||
         world > tqkv::kMaxPeers || rank < 0 || rank >= world)
         return TQKV_ERR_INVALID_SIZE;
     if (!q || !k_new || !v_new || !kq || !ks || !vq || !vs || !exchange_bufs) return TQKV_ERR_NULL;
+    if (kind == OutKind::kExchange && !o) return TQKV_ERR_NULL;
     if (!tqkv::aligned16(kq) || !tqkv::aligned16(vq) || !tqkv::aligned16(k_new) ||
         !tqkv::aligned16(v_new))
         return TQKV_ERR_MISALIGNED;
@@ -782,8 +843,49 @@ tqkv_status tqkv_decode_int8_append_publish(const void* q, const void* k_new, co
     const tqkv_status pst = tqkv::make_peer_args(exchange_bufs, world, rank, &peer);
     if (pst != TQKV_OK) return pst;
     const tqkv::AppendRows rows{k_new, v_new, T};
-    return tqkv::launch_decode_peers(peer, q, kq, ks, vq, vs, static_cast<int>(BH), S, D,
+    return tqkv::launch_decode_peers(kind, peer, q, kq, ks, vq, vs, o, static_cast<int>(BH), S, D,
                                      block_size, workspace, workspace_bytes, stream, S_cap, &rows);
+}
+}  // namespace
+
+tqkv_status tqkv_decode_int8_publish(const void* q, const int8_t* kq, const void* ks,
+                                     const int8_t* vq, const void* vs, int B, int H, int S, int D,
+                                     int block_size, void* workspace, size_t workspace_bytes,
+                                     void* const* exchange_bufs, int world, int rank,
+                                     cudaStream_t stream) {
+    return decode_split_step(OutKind::kPeers, q, kq, ks, vq, vs, nullptr, B, H, S, D, block_size,
+                             workspace, workspace_bytes, exchange_bufs, world, rank, stream);
+}
+
+tqkv_status tqkv_decode_int8_exchange(const void* q, const int8_t* kq, const void* ks,
+                                      const int8_t* vq, const void* vs, void* o, int B, int H,
+                                      int S, int D, int block_size, void* workspace,
+                                      size_t workspace_bytes, void* const* exchange_bufs,
+                                      int world, int rank, cudaStream_t stream) {
+    return decode_split_step(OutKind::kExchange, q, kq, ks, vq, vs, o, B, H, S, D, block_size,
+                             workspace, workspace_bytes, exchange_bufs, world, rank, stream);
+}
+
+tqkv_status tqkv_decode_int8_append_publish(const void* q, const void* k_new, const void* v_new,
+                                            int8_t* kq, void* ks, int8_t* vq, void* vs, int B,
+                                            int H, int T, int S, int S_cap, int D, int block_size,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* const* exchange_bufs, int world, int rank,
+                                            cudaStream_t stream) {
+    return decode_split_step_append(OutKind::kPeers, q, k_new, v_new, kq, ks, vq, vs, nullptr, B,
+                                    H, T, S, S_cap, D, block_size, workspace, workspace_bytes,
+                                    exchange_bufs, world, rank, stream);
+}
+
+tqkv_status tqkv_decode_int8_append_exchange(const void* q, const void* k_new, const void* v_new,
+                                             int8_t* kq, void* ks, int8_t* vq, void* vs, void* o,
+                                             int B, int H, int T, int S, int S_cap, int D,
+                                             int block_size, void* workspace,
+                                             size_t workspace_bytes, void* const* exchange_bufs,
+                                             int world, int rank, cudaStream_t stream) {
+    return decode_split_step_append(OutKind::kExchange, q, k_new, v_new, kq, ks, vq, vs, o, B, H,
+                                    T, S, S_cap, D, block_size, workspace, workspace_bytes,
+                                    exchange_bufs, world, rank, stream);
 }
 
 tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o, int world, int rank,
@@ -866,13 +968,12 @@ extern "C" tqkv_status tqkv_decode_int8_noalloc(const void* q, const int8_t* kq,
     void* scratch = nullptr;
     tqkv_status st = tqkv::noalloc_scratch_address(&scratch);
     if (st != TQKV_OK) return st;
-    // The array keeps whatever the previous call left.  Only the scheduler and
-    // ticket counters at its start must be zero when a launch begins (partial
-    // records are always written before they are read); a completed call
-    // leaves them zero, an interrupted one might not, so clear them every time.
-    const size_t counter_bytes = tqkv::decode_ws_counter_bytes(BH);
+    // The array keeps whatever the previous call left.  A launch needs the
+    // counters at its start and the records of this shape at zero (a record
+    // whose values are tagged counts as stored); a completed call leaves them
+    // zero, an interrupted one might not, so clear them every time.
     if (need > 0) {
-        st = tqkv::from_cuda(cudaMemsetAsync(scratch, 0, counter_bytes, stream));
+        st = tqkv::from_cuda(cudaMemsetAsync(scratch, 0, need, stream));
         if (st != TQKV_OK) return st;
     }
     return tqkv::launch_decode(tqkv::KvKind::kInt8, tqkv::OutKind::kHalfO, q, kq, ks, vq, vs, o,

@@ -11,7 +11,7 @@
 namespace tqkv {
 
 enum class KvKind : int { kInt8 = 0, kHalf = 1 };
-enum class OutKind : int { kHalfO = 0, kPartial = 1, kPeers = 2 };
+enum class OutKind : int { kHalfO = 0, kPartial = 1, kPeers = 2, kExchange = 3 };
 
 // Records `err` as this host thread's last CUDA error and returns
 // TQKV_ERR_CUDA, or returns TQKV_OK for cudaSuccess.
@@ -50,9 +50,6 @@ tqkv_status launch_empty_partials(float* p, long long heads, int D, cudaStream_t
 
 // Workspace bytes the decode kernels need for (BH, S, D) on the current device.
 size_t decode_workspace_bytes(long long BH, int S, int D);
-// Bytes at the start of a decode workspace that hold counters (scheduler and
-// per-head tickets); the rest is partial records, written before being read.
-size_t decode_ws_counter_bytes(long long BH);
 
 // Per-(device, stream) grow-only workspace used by the reference-signature
 // launchers, which have no workspace argument (ws_cache.h).  Zero-filled on

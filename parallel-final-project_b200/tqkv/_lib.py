@@ -68,6 +68,12 @@ C_ABI = {
     "tqkv_decode_int8_append_publish": (c_int, [c_void_p] * 7 + [c_int] * 7 +
                                         [c_void_p, c_size_t, ctypes.POINTER(c_void_p), c_int,
                                          c_int, c_void_p]),
+    "tqkv_decode_int8_exchange": (c_int, [c_void_p] * 6 + [c_int] * 5 +
+                                  [c_void_p, c_size_t, ctypes.POINTER(c_void_p), c_int, c_int,
+                                   c_void_p]),
+    "tqkv_decode_int8_append_exchange": (c_int, [c_void_p] * 8 + [c_int] * 7 +
+                                         [c_void_p, c_size_t, ctypes.POINTER(c_void_p), c_int,
+                                          c_int, c_void_p]),
 }
 
 # The reference's C++ launchers (include/attention.h, include/quantization.h),

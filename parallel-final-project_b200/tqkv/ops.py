@@ -179,22 +179,32 @@ class Workspace:
     """A zero-initialised decode workspace on one device, grown on demand.
 
     The kernels leave it zeroed after every call, so one Workspace can serve
-    any number of calls that are ordered on the same stream.
+    any number of calls that are ordered on the same stream.  A buffer once
+    handed out is never freed while the Workspace lives: when a larger shape
+    needs more, the old buffer is retired and kept, so a CUDA graph captured
+    with it stays valid (torch.cuda.graph empties the allocator's cache when a
+    capture begins, which would otherwise unmap a freed workspace under an
+    earlier graph).  Growth at least doubles, so retired buffers add up to
+    less than the live one.
     """
 
     def __init__(self, device=None):
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
         self.buf: Optional[torch.Tensor] = None
+        self._retired: list = []
 
     def get(self, nbytes: int, stream=None) -> Tuple[Optional[int], int]:
         if nbytes == 0:
             return None, 0
         if self.buf is None or self.buf.numel() < nbytes:
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            size = nbytes if self.buf is None else max(nbytes, 2 * self.buf.numel())
+            if self.buf is not None:
+                self._retired.append(self.buf)
+            self.buf = torch.empty(size, dtype=torch.uint8, device=self.device)
             lib = load()
             check("tqkv_workspace_init", lib.tqkv_workspace_init(
-                self.buf.data_ptr(), nbytes, _stream_handle(stream)))
+                self.buf.data_ptr(), size, _stream_handle(stream)))
         return self.buf.data_ptr(), self.buf.numel()
 
 

@@ -11,6 +11,11 @@ into every other rank's buffer.  Per decode step:
     combine(out)   bounded wait until this rank's buffer holds every rank's
                    entries of this step, merge into O, advance the step
 
+or both in one cooperative launch, step(..., out) (step_append with the
+newest tokens appended): after its share of the slice, each CTA of the decode
+launch merges heads whose records have arrived from every rank, so the
+exchange overlaps the other CTAs' streaming and no second launch is needed.
+
 A rank that stops stepping makes the others' combines time out (device error
 flag); tqkv.health.StepMonitor detects it on the host between steps.
 
@@ -93,6 +98,46 @@ class PeerExchange:
             vq.data_ptr(), vs.data_ptr(), B, H, T, S, S_cap, D, block_size, wptr, wbytes,
             self.bufs, self.world, self.rank, _stream_handle(stream)))
 
+    def step(self, q, kq, ks, vq, vs, block_size: int, out: torch.Tensor,
+             workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+        """publish() and combine(out) in one launch (tqkv_decode_int8_exchange);
+        the same O, bit for bit."""
+        B, H, S, D = _check_int8_kv(kq, ks, vq, vs, block_size)
+        if B * H != self.BH or D != self.D:
+            raise ValueError(f"exchange is for BH={self.BH} D={self.D}, got {B * H} x {D}")
+        _need(q, "q", B * H * D, 2, kq)
+        _need(out, "out", B * H * D, 2, kq)
+        ws = _workspace(workspace, q.device)
+        wptr, wbytes = ws.get(workspace_bytes(B, H, max(S, 1), D), stream)
+        check("tqkv_decode_int8_exchange", load().tqkv_decode_int8_exchange(
+            q.data_ptr(), kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
+            out.data_ptr(), B, H, S, D, block_size, wptr, wbytes, self.bufs, self.world,
+            self.rank, _stream_handle(stream)))
+        return out
+
+    def step_append(self, q, k_new, v_new, kq, ks, vq, vs, S: int, block_size: int,
+                    out: torch.Tensor, workspace: Optional[Workspace] = None,
+                    stream=None) -> torch.Tensor:
+        """publish_append() and combine(out) in one launch
+        (tqkv_decode_int8_append_exchange)."""
+        B, H, S_cap, D = _check_int8_kv(kq, ks, vq, vs, block_size)
+        if B * H != self.BH or D != self.D:
+            raise ValueError(f"exchange is for BH={self.BH} D={self.D}, got {B * H} x {D}")
+        Bn, Hn, T, Dn = _bhsd(k_new, "k_new")
+        if (Bn, Hn, Dn) != (B, H, D) or v_new.shape != k_new.shape:
+            raise ValueError("k_new and v_new must be [B, H, T, D] matching the caches")
+        for t, n in ((k_new, "k_new"), (v_new, "v_new")):
+            _need(t, n, B * H * T * D, 2, kq)
+        _need(q, "q", B * H * D, 2, kq)
+        _need(out, "out", B * H * D, 2, kq)
+        ws = _workspace(workspace, q.device)
+        wptr, wbytes = ws.get(workspace_bytes(B, H, S, D), stream)
+        check("tqkv_decode_int8_append_exchange", load().tqkv_decode_int8_append_exchange(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), kq.data_ptr(), ks.data_ptr(),
+            vq.data_ptr(), vs.data_ptr(), out.data_ptr(), B, H, T, S, S_cap, D, block_size,
+            wptr, wbytes, self.bufs, self.world, self.rank, _stream_handle(stream)))
+        return out
+
     def combine(self, out: torch.Tensor, stream=None) -> torch.Tensor:
         _need(out, "out", self.BH * self.D, 2, out)
         check("tqkv_exchange_combine", load().tqkv_exchange_combine(
@@ -133,6 +178,8 @@ class LocalExchange:
     publish = PeerExchange.publish
     publish_append = PeerExchange.publish_append
     combine = PeerExchange.combine
+    step = PeerExchange.step
+    step_append = PeerExchange.step_append
 
     def close(self) -> None:
         if self.own is not None:

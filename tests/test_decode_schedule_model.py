@@ -93,6 +93,7 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0, group=1)
         r0, r1 = c * R, min((c + 1) * R, total)
         assert r0 < r1
         r = r0
+        firsts = 0
         while r < r1:
             bh = r // S
             head0 = bh * S
@@ -143,8 +144,14 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0, group=1)
                     assert (qsrc & 15) + D * 2 <= qslot
             c_first, c_last = head0 // R, (head0 + S - 1) // R
             assert 0 <= c - c_first < c_last - c_first + 1 <= maxp
+            if c == c_first and c_last > c_first:   # the first piece of a cut head:
+                firsts += 1                         # merged at the end of its CTA
             covered += tb - ta
             r = head0 + tb
+        # each chunk leaves its CTA at most one cut head to merge, and a CTA
+        # claims at most kMaxDefer chunks, which covers every chunk
+        assert firsts <= 1
+    assert nchunks <= grid * _const("decode_attn.cuh", "kMaxDefer") // 4
     assert covered == total
 
 
@@ -173,12 +180,15 @@ def test_schedule_in_bounds_with_cache_stride(D, bs):
 
 def test_stage_layout_fits_four_ctas_per_sm():
     """3-stage ring + merge scratch + barriers + tile descriptors + control
-    block of the largest instantiation (INT8, D = 128, bs = 32) leave room for
-    four CTAs in 228 KB."""
-    RB, nsub = 128, 4
+    block + list of cut heads to merge, of the largest instantiation (INT8,
+    D = 128, bs = 32), leave room for four CTAs in 228 KB."""
+    RB, nsub, D = 128, 4, 128
     TILE = TILE_BYTES // RB
-    stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (128 * 2 + 32)
-    smem = STAGES * stage + WARPS * (128 + 2) * 4 + 2 * STAGES * 8 + STAGES * 32 + 32
+    defer = _const("decode_attn.cuh", "kMaxDefer")
+    stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (D * 2 + 32)
+    slices = WARPS * 32 // (D // 4)
+    merge = -(-max(WARPS * (D + 2), slices * (D + 4)) * 4 // 16) * 16
+    smem = STAGES * stage + merge + 2 * STAGES * 8 + STAGES * 32 + 32 + defer * 8
     assert 4 * (smem + 1024) <= 228 * 1024, smem
 
 
@@ -249,3 +259,16 @@ def test_exchange_buffer_holds_every_entry():
                 assert last + 8 <= nbytes, (world, BH, D)
     assert lib.tqkv_exchange_bytes(peers + 1, 4, 128) == 0
     assert lib.tqkv_exchange_bytes(2, 4, 96) == 0
+
+
+def test_exchange_merge_counters_fit_the_scheduler_area():
+    """The one-launch exchange keeps its two merge counters (heads claimed,
+    CTAs finished) after the two chunk-scheduler counters, before the
+    records of the pieces of cut heads (which start on 16 bytes)."""
+    src = open(os.path.join(CSRC, "tqkv_capi.cu")).read()
+    m = re.search(r"a\.fold = reinterpret_cast<unsigned int\*>\(ws \+ lay\.sched_off\) \+ (\d+);", src)
+    assert m, "fold counter placement"
+    first = int(m.group(1))
+    recs = re.search(r"w\.parts_off = (\d+);", src)
+    assert recs
+    assert first >= 2 and 4 * (first + 2) <= int(recs.group(1)) and int(recs.group(1)) % 16 == 0

@@ -221,13 +221,14 @@ def test_workspace_left_zeroed():
     torch.cuda.synchronize()
     nb = tqkv.workspace_bytes(B, H, S, D)
     assert nb > 0
-    # tickets and every partial record: the whole workspace is zero again
+    # counters and every piece record: the whole workspace is zero again
     assert int(ws.buf.count_nonzero()) == 0
 
 
 def test_workspace_reused_across_shapes():
-    """One workspace serves calls of different shapes in any order: a call's
-    ticket counters never see records left by an earlier, smaller call."""
+    """One workspace serves calls of different shapes in any order: a call
+    never takes a record left by an earlier call for one of its own pieces
+    (every call leaves the records zero)."""
     ws = tqkv.Workspace()
     shapes = [(1, 2, 40000, 128, 128), (8, 12, 3000, 64, 64), (1, 1, 90000, 128, 32),
               (4, 32, 2500, 128, 64), (1, 3, 70000, 64, 32)]

@@ -3,8 +3,11 @@ runs the partial kernel, the records are all-gathered over NCCL and merged by
 the LSE combine kernel on every rank; and the same split over NVLink peer
 mappings (publish + combine, no NCCL) for several consecutive steps, also
 with the newest token appended inside the last rank's publish launch.  All
-must equal the one-GPU decode of the whole sequence.  Runs as one child process per GPU (2 to 4
-GPUs, NCCL with NVLS off); skipped when fewer than 2 GPUs are visible."""
+must equal the one-GPU decode of the whole sequence, and the NVLink steps,
+two-launch (publish + combine) and one-launch (tqkv_decode_int8_exchange)
+alternating, must give every rank the same O bit for bit.  Runs as one child
+process per GPU (2 to 4 GPUs, NCCL with NVLS off); skipped when fewer than 2
+GPUs are visible."""
 import datetime
 import os
 import socket
@@ -57,17 +60,24 @@ def _rank_main(rank, world, port, q_out):
         # the same split over NVLink peer mappings (no NCCL), several steps
         ex = tqkv.PeerExchange(world, rank, w.BH, w.D)
         try:
-            for step in range(4):
+            for step in range(8):
                 qs = (q.float() * (1.0 + 0.25 * step)).half()
-                ex.publish(qs, kq, ks, vq, vs, w.block_size)
-                o2 = ex.combine(torch.empty_like(o))
+                if step % 2 == 0:      # two launches: publish, then combine
+                    ex.publish(qs, kq, ks, vq, vs, w.block_size)
+                    o2 = ex.combine(torch.empty_like(o))
+                else:                  # one cooperative launch
+                    o2 = ex.step(qs, kq, ks, vq, vs, w.block_size, torch.empty_like(o))
                 ref2 = tqkv.decode_int8(qs, kqf, ksf, vqf, vsf, w.block_size)
                 torch.cuda.synchronize()
                 err = max(err, (o2.float() - ref2.float()).abs().max().item())
+                # every rank merges the same records in the same order
+                allo = [torch.empty_like(o2) for _ in range(world)]
+                dist.all_gather(allo, o2)
+                assert all(torch.equal(a, o2) for a in allo), step
             # decode loop: the rank holding the sequence end appends each new
             # token inside its publish launch; reference: the one-GPU fused
             # append + decode over the whole, growing cache
-            steps, S_loc = 3, s1 - s0
+            steps, S_loc = 4, s1 - s0
             last = rank == world - 1
 
             def grow(t, rows):
@@ -82,11 +92,18 @@ def _rank_main(rank, world, port, q_out):
                 kn = torch.randn((w.B, w.H, 1, w.D), generator=gen, device=dev).half()
                 vn = torch.randn((w.B, w.H, 1, w.D), generator=gen, device=dev).half()
                 qs = torch.randn((w.B, w.H, w.D), generator=gen, device=dev).half()
-                if last:
-                    ex.publish_append(qs, kn, vn, *mine, S_loc + i + 1, w.block_size)
+                one_launch = i % 2 == 1
+                if last and one_launch:
+                    o3 = ex.step_append(qs, kn, vn, *mine, S_loc + i + 1, w.block_size,
+                                        torch.empty_like(o))
+                elif one_launch:
+                    o3 = ex.step(qs, kq, ks, vq, vs, w.block_size, torch.empty_like(o))
                 else:
-                    ex.publish(qs, kq, ks, vq, vs, w.block_size)
-                o3 = ex.combine(torch.empty_like(o))
+                    if last:
+                        ex.publish_append(qs, kn, vn, *mine, S_loc + i + 1, w.block_size)
+                    else:
+                        ex.publish(qs, kq, ks, vq, vs, w.block_size)
+                    o3 = ex.combine(torch.empty_like(o))
                 ref3 = tqkv.decode_int8_append(qs, kn, vn, *whole, w.S + i + 1, w.block_size)
                 torch.cuda.synchronize()
                 err = max(err, (o3.float() - ref3.float()).abs().max().item())
