@@ -101,10 +101,9 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
  * The B*H*S token rows are cut into fixed chunks: one per CTA, or, for very
  * long runs per CTA, about eight per CTA claimed from a counter in
  * `workspace`.  A head that spans several chunks leaves one record per piece
- * in `workspace`; the CTA that streamed its first piece merges them
- * (log-sum-exp, in piece order: results do not depend on which CTA streamed
- * which chunk) once it has streamed all of its own chunks.  Kernel launches
- * are cooperative (every CTA resident).  Size the workspace with
+ * in `workspace`; CTAs that have no chunk left merge them (log-sum-exp, in
+ * piece order: results do not depend on which CTA streamed which chunk).
+ * Size the workspace with
  * tqkv_decode_workspace_bytes() and zero it once with tqkv_workspace_init()
  * before its first use; every decode call leaves it zeroed again (after a
  * device error, zero it again).  Calls that share one workspace must be
@@ -273,10 +272,8 @@ tqkv_status tqkv_exchange_combine(void* const* exchange_bufs, void* o,
  * share of the token slice, each CTA takes heads from a counter in the
  * workspace, waits (bounded, ~1 s) for every rank's records of the head,
  * merges them and writes O; the last CTA to finish advances this rank's step
- * counter.  The launch is cooperative (every CTA resident), because a CTA may
- * wait for records that another CTA of the same launch emits.  Same O as the
- * two-launch pair, bit for bit, with the same buffers and record slots: a
- * sequence of steps may use either form, step by step.  S == 0 (a rank whose
+ * counter.  Same O as the two-launch pair, bit for bit, with the same buffers
+ * and record slots: a sequence of steps may use either form, step by step.  S == 0 (a rank whose
  * slice is empty) publishes empty records and merges with two small launches.
  * A wait that runs out leaves NaN in that head's O and sets the device error
  * flag; after a device error, re-zero the workspace (tqkv_workspace_init) and

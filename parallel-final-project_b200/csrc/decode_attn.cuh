@@ -11,21 +11,21 @@
 // never written back).
 //
 // Work split ("flat split-S").  The B*H*S token rows, heads laid end to end,
-// are cut into fixed chunks of C rows: one chunk per CTA (C = ceil(B*H*S /
-// grid)), so every CTA streams the same number of bytes whatever B, H and S
-// are; or, when a CTA would stream very many rows, ~8 chunks per CTA that the
-// CTAs claim from a counter in the workspace.  A chunk covers the tail of one
+// are cut into fixed chunks of C rows: about one chunk per CTA (C =
+// ceil(B*H*S / grid)), so every CTA streams the same number of bytes whatever
+// B, H and S are; or, when a CTA would stream very many rows, ~8 chunks per
+// CTA.  Either way the CTAs claim chunks from a counter in the workspace.  A chunk covers the tail of one
 // head, whole heads, and the head of another; each piece ("segment") yields an
 // online-softmax state (m, l, acc[D]).  A head that lies inside one chunk is
 // finished there.  A head cut across chunks has every piece store its state
 // to the workspace as a record whose values carry a presence tag (no fence,
-// no atomic); the CTA that holds the head's first piece (the end of one of
-// its chunks) merges the head's records by log-sum-exp after it has streamed
-// all of its own chunks, and writes O.  Every CTA stores all of its records
-// before it waits for anyone else's, and the launch is cooperative (every CTA
-// resident), so the waits always end.  The merge zeroes the records it read
-// and the last producer resets the claim counter, so the workspace stays
-// zeroed between calls.
+// no atomic).  A CTA whose producer has found no chunk left claims cut heads
+// from a second counter and merges each head's records by log-sum-exp, in
+// piece order, then writes O.  It waits only for pieces of chunks that other
+// CTAs have already claimed (the pool is empty) and that those CTAs stream
+// without waiting for anyone, so every wait ends, whatever CTAs are resident.
+// The merge zeroes the records it read and the last CTA of the launch resets
+// the counters, so the workspace stays zeroed between calls.
 //
 // CTA = 4 consumer warps + 1 producer warp.  One producer lane streams tiles
 // of TILE tokens (K rows, V rows, their fp16 scales, and q at the start of a
@@ -72,10 +72,6 @@ constexpr int kDecodeConsumers = kDecodeConsumerWarps * 32;
 constexpr int kDecodeThreads = kDecodeConsumers + 32;
 constexpr int kDecodeTileBytes = 8192;  // bytes of K (and of V) per stage
 constexpr int kDecodeStages = 3;        // 3 stages x ~17.7 KB: four CTAs fit on an SM
-// Cut heads whose first piece one CTA holds, merged at its end: at most one
-// per chunk, so a CTA claims at most this many chunks (the plan hands out
-// far fewer per CTA on average).
-constexpr int kMaxDefer = 32;
 
 enum DecodeOut : int {
     kOutHalf = 0,     // write O (fp16)
@@ -83,7 +79,7 @@ enum DecodeOut : int {
     kOutPeers = 2,    // write the records, tagged with the step number, into every
                       // rank's exchange buffer (split-S over NVLink)
     kOutExchange = 3, // kOutPeers, then merge every rank's records into O in the
-                      // same launch (cooperative: see exchange_epilogue)
+                      // same launch (exchange_epilogue)
 };
 
 // Exchange buffer of one rank (split-S across the GPUs of a node), written by
@@ -141,7 +137,9 @@ struct DecodeArgs {
     long long total_rows;      // BH * S
     long long chunk_rows;      // C: chunk u is rows [u * C, (u + 1) * C) of the BH * S rows
     unsigned int nchunks;      // ceil(total_rows / C)
-    unsigned int* sched;       // workspace: [0] next chunk to hand out, [1] producers done
+    unsigned int* ctr;         // workspace counters: [0] next chunk to hand out, [1] cut heads
+                               // claimed for merging, [2] heads claimed for the exchange merge,
+                               // [3] CTAs finished; null when one CTA streams everything
     int S;                     // rows attended per head
     int S_stride;              // rows between consecutive heads in K/V/scales (>= S)
     int group;                 // query heads per K/V head (GQA/MQA; 1 = one K/V head each)
@@ -152,8 +150,6 @@ struct DecodeArgs {
     const void* k_new;         // fused append only: fp16 [BH][T_new][D], rows [S - T_new, S)
     const void* v_new;
     int T_new;
-    unsigned int* fold;        // kOutExchange: workspace [0] heads claimed for merging,
-                               // [1] CTAs finished
 };
 
 template <int D, int BS, bool kHalfKV>
@@ -196,8 +192,7 @@ struct DecodeCfg {
     static constexpr int kOffBars = kOffMerge + kMergeBytes;
     static constexpr int kOffMeta = kOffBars + 2 * kDecodeStages * 8;  // int[stages][8]
     static constexpr int kOffCtl = kOffMeta + kDecodeStages * 32;      // CtaCtl
-    static constexpr int kOffDefer = kOffCtl + 32;                     // int2[kMaxDefer]
-    static constexpr int kSmemBytes = kOffDefer + kMaxDefer * 8;
+    static constexpr int kSmemBytes = kOffCtl + 32;
 
     static_assert(kTPG == 4, "each lane group owns 4 rows per stage");
     static_assert(kStageBytes % 16 == 0, "stage must stay 16-byte aligned");
@@ -213,15 +208,13 @@ struct TileMeta {
     int pad;
 };
 
-// CTA control block in shared memory: the claim slot of the exchange
-// epilogue, an abort flag that a warp whose bounded wait ran out raises so
-// that the others leave as well, and the count of cut heads this CTA merges
-// at its end (listed after the block as (head, pieces) pairs).
+// CTA control block in shared memory: the slot through which thread 0 hands
+// a claimed head to the other consumer threads, and an abort flag that a warp
+// whose bounded wait ran out raises so that the others leave as well.
 struct CtaCtl {
     int flag;
     unsigned int abort;
-    int ndefer;
-    unsigned int pad[5];
+    unsigned int pad[6];
 };
 static_assert(sizeof(CtaCtl) == 32, "CtaCtl layout");
 
@@ -379,23 +372,21 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
     uint32_t phase = 0;
     long long issued = 0;
     bool ok = true;
-    // Chunks are taken statically (chunk = blockIdx.x) or, with a scheduler,
-    // handed out dynamically so that SMs that stream faster take more of them.
-    // Chunk boundaries are fixed either way, which keeps the pieces of a split
-    // head (and their indices) deterministic.  A chunk may cover the end of
-    // one head and the start of the next: one segment per head.
-    unsigned int static_chunk = blockIdx.x;  // without a scheduler (sched == nullptr)
-    int claimed = 0;
+    // Chunks are claimed from a counter, so SMs that stream faster take more
+    // of them, and every chunk has been claimed by a running CTA before any
+    // CTA starts waiting for merges (see merge_epilogue).  Chunk boundaries
+    // are fixed, which keeps the pieces of a split head (and their indices)
+    // deterministic.  A chunk may cover the end of one head and the start of
+    // the next: one segment per head.  Without counters (one CTA, one chunk)
+    // the CTA takes chunk 0.
+    bool took_only_chunk = false;
     while (ok) {
         unsigned int chunk;
-        if (a.sched != nullptr) {
-            // each chunk may leave this CTA one cut head to merge at its end
-            if (claimed == kMaxDefer) break;
-            ++claimed;
-            chunk = atomicAdd(&a.sched[0], 1u);
+        if (a.ctr != nullptr) {
+            chunk = atomicAdd(&a.ctr[0], 1u);
         } else {
-            chunk = static_chunk;
-            static_chunk += gridDim.x;
+            chunk = took_only_chunk ? a.nchunks : 0u;
+            took_only_chunk = true;
         }
         if (chunk >= a.nchunks) break;
         const long long c0 = static_cast<long long>(chunk) * a.chunk_rows;
@@ -508,14 +499,6 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             record_device_error(kErrEmptyWaitTimeout);
             atomicExch(&ctl->abort, 1u);
         }
-    }
-    // the last producer to finish hands the scheduler back zeroed: every
-    // producer has taken its final (empty) chunk before counting itself out
-    __threadfence();
-    if (a.sched != nullptr && atomicAdd(&a.sched[1], 1u) == gridDim.x - 1) {
-        __threadfence();
-        atomicExch(&a.sched[0], 0u);
-        atomicExch(&a.sched[1], 0u);
     }
     // Drain: do not leave the CTA while copies into its shared memory are in
     // flight.  In a normal run every stage was consumed long ago.
@@ -815,11 +798,44 @@ __device__ __forceinline__ void lse_factors(float m, float mo, float& M, float& 
     fb = fast_exp2(mo - base);
 }
 
+// Pause between polls of records that have not arrived: from kPollNapMinNs,
+// doubling up to kPollNapMaxNs.  Waiting CTAs then load little from L2 while
+// the CTAs still streaming KV need it, and notice an arrival within ~0.5 us.
+constexpr unsigned int kPollNapMinNs = 32;
+constexpr unsigned int kPollNapMaxNs = 512;
+__device__ __forceinline__ void poll_nap(unsigned int& ns) {
+    __nanosleep(ns);
+    ns = ns < kPollNapMaxNs ? 2 * ns : kPollNapMaxNs;
+}
+
+// Called by the 32 lanes of one warp: waits (bounded, napping between rounds)
+// until the 64-bit values first[i * stride], i < n, all carry `tag` in their
+// high word.  One value per record is watched, one lane per record, before
+// the CTA loads whole records: far fewer L2 requests than every thread
+// polling every value it needs.  Gives up silently after ~2^31 SM cycles (the
+// per-value polls that follow time out and report).
+__device__ __forceinline__ void lanes_wait_tagged(const unsigned long long* first, long long stride,
+                                                  int n, unsigned int tag) {
+    const int lane = threadIdx.x & 31;
+    const long long start = clock64();
+    unsigned int nap = kPollNapMinNs;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        bool ok = i >= n || static_cast<unsigned int>(ld_volatile_u64(first + i * stride) >> 32) == tag;
+        while (!__all_sync(0xffffffffu, ok)) {
+            if (clock64() - start > (1ll << 31)) return;
+            poll_nap(nap);
+            if (!ok) ok = static_cast<unsigned int>(ld_volatile_u64(first + i * stride) >> 32) == tag;
+        }
+    }
+}
+
 // Merge the `world` records of head bh for `step` from this rank's exchange
 // buffer into O[bh][t] (one thread per dim t < D), natural-log units.  Every
 // load of the thread's 3 * world entries is issued at once (one round trip
 // when the peers are done, the usual case); only entries still carrying an
-// older step are polled again, for at most ~2^31 SM cycles (about a second).
+// older step are polled again (poll_nap between rounds), for at most ~2^31 SM
+// cycles (about a second).
 // On timeout the device error flag gets kErrPeerWaitTimeout and O[bh][t] is
 // NaN, so a lost peer shows in the output as well.
 template <int D>
@@ -844,7 +860,9 @@ __device__ __forceinline__ void combine_head(const PeerArgs& p, int BH, int bh, 
     if (!ready) {
         const long long start = clock64();
 #pragma unroll 1
+        unsigned int nap = kPollNapMinNs;
         for (uint32_t it = 0; it < (1u << 30) && !ready; ++it) {
+            poll_nap(nap);
             ready = true;
 #pragma unroll
             for (int r = 0; r < kMaxPeers; ++r) {
@@ -932,8 +950,7 @@ __device__ __forceinline__ void emit_head(const DecodeArgs& a, int bh, int tid, 
 
 // Finish one segment: merge the lane-group states of the CTA, then either
 // write O / the partial record (head held by one chunk), or store the piece's
-// tagged record for the head's merge (merge_cut_head, run at the end of the
-// CTA that holds part 0, which this call lists when it is that part).
+// tagged record for the head's merge (merge_cut_head).
 // Returns false when a consumer barrier gave up (the CTA then leaves).
 template <int D, int BS, bool kHalfKV, int OUT>
 __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, const DecodeArgs& a,
@@ -1003,32 +1020,23 @@ __device__ __forceinline__ bool finish_segment(SegState<D, BS, kHalfKV>& st, con
     }
 
     // A piece of a head cut across chunks: store its record, every value
-    // tagged as present, and go on streaming.  The CTA holding the head's
-    // first piece merges all of them once it has streamed all of its chunks.
+    // tagged as present, and go on streaming; the head is merged by a CTA
+    // that has finished streaming (merge_epilogue).
     unsigned long long* rec =
         a.recs + (static_cast<long long>(bh) * a.max_parts + part) * C::kRecWords;
     if (tid < D) st_relaxed_u64(rec + tid, tag_present(A));
     if (tid == 0) {
         st_relaxed_u64(rec + D, tag_present(M));
         st_relaxed_u64(rec + D + 1, tag_present(L));
-        if (part == 0) {
-            int2* defer = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(ctl) + 32);
-            const int n = ctl->ndefer;
-            if (n < kMaxDefer) {
-                defer[n] = make_int2(bh, nparts);
-                ctl->ndefer = n + 1;
-            } else {
-                record_device_error(kErrDeferOverflow);
-            }
-        }
     }
-    // merge[] (and the list) are reused by the next segment
+    // merge[] is reused by the next segment
     return consumer_barrier(ctl);
 }
 
 // Merge the `nparts` records of cut head bh (log-sum-exp, in part order, so
 // the result does not depend on which CTA streamed which piece) and emit the
-// head.  Threads take 4 dims each (kRecLanes per record) and one slice of the
+// head.  Warp 0 first waits until every record's m value is stored; then
+// threads take 4 dims each (kRecLanes per record) and one slice of the
 // records (parts sl, sl + kRecSlices, ...), loading 4 parts at a time and
 // polling, bounded (~2^31 SM cycles), only values whose tag is not yet set;
 // the slices' states are then merged through shared memory.  The records are
@@ -1044,6 +1052,9 @@ __device__ __forceinline__ bool merge_cut_head(const DecodeArgs& a, float* merge
     const int sl = tid / C::kRecLanes;   // records sl, sl + kRecSlices, ...
     const unsigned long long* recs =
         a.recs + static_cast<long long>(bh) * a.max_parts * C::kRecWords;
+    // warp 0 watches each record's m value until every piece has stored it
+    if (tid < 32) lanes_wait_tagged(recs + D, C::kRecWords, nparts, 1u);
+    if (!consumer_barrier(ctl)) return false;
     float M = -INFINITY, L = 0.0f;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const long long start = clock64();
@@ -1068,12 +1079,14 @@ __device__ __forceinline__ bool merge_cut_head(const DecodeArgs& a, float* merge
             const unsigned long long* r = recs + p * C::kRecWords;
             // poll only what has not arrived yet
 #pragma unroll 1
+            unsigned int nap = kPollNapMinNs;
             while (!(is_present(ml[j].x) && is_present(ml[j].y) && is_present(a01[j].x) &&
                      is_present(a01[j].y) && is_present(a23[j].x) && is_present(a23[j].y))) {
                 if (late || clock64() - start > (1ll << 31)) {
                     late = true;
                     break;
                 }
+                poll_nap(nap);
                 if (!(is_present(ml[j].x) && is_present(ml[j].y))) ml[j] = ld_relaxed_u64x2(r + D);
                 if (!(is_present(a01[j].x) && is_present(a01[j].y))) a01[j] = ld_relaxed_u64x2(r + 4 * dq);
                 if (!(is_present(a23[j].x) && is_present(a23[j].y)))
@@ -1125,36 +1138,73 @@ __device__ __forceinline__ bool merge_cut_head(const DecodeArgs& a, float* merge
     return consumer_barrier(ctl);  // merge[] is reused by the next merge
 }
 
-// kOutExchange, after a CTA's last segment: the CTA claims heads from a
-// counter and merges every rank's records of each into O (combine_head), then
-// counts itself out; the last CTA of the launch resets the counters and
-// advances this rank's step.  A claimed head's records come from every rank,
-// this one included, i.e. from other CTAs of this launch, so the launch must
-// be cooperative (every CTA resident; the plan's grid never exceeds the
-// resident CTAs).  Across ranks nothing is circular: each rank emits all of
-// its records of the step before any of its CTAs waits.  Returns false when a
+// After its last chunk a CTA claims cut heads from ctr[1] and merges them
+// (merge_cut_head).  Its producer has found the chunk pool empty, so every
+// chunk is held by a CTA that streams it and stores its records without
+// waiting for anyone: the waits end whichever CTAs are resident, and no
+// cooperative launch is needed.  Candidates are the heads when a chunk is no
+// longer than a head (uncut heads are skipped), else the interior chunk
+// boundaries, each of which cuts at most one head.  Returns false when a
 // consumer barrier gave up.
-template <int D>
-__device__ __forceinline__ bool exchange_epilogue(const DecodeArgs& a, CtaCtl* ctl, int tid) {
-    const unsigned int step = __ldcg(a.peer.own + kHdrEpoch) + 1u;
-    __half* o = static_cast<__half*>(a.out);
+template <int D, int BS, bool kHalfKV, int OUT>
+__device__ __forceinline__ bool merge_epilogue(const DecodeArgs& a, float* merge, CtaCtl* ctl,
+                                               int tid) {
+    const long long C = a.chunk_rows;
+    const bool by_head = C <= a.S;
+    const long long ncand = by_head ? static_cast<long long>(a.BH)
+                                    : static_cast<long long>(a.nchunks) - 1;
     for (;;) {
-        if (tid == 0) ctl->flag = static_cast<int>(atomicAdd(&a.fold[0], 1u));
+        if (tid == 0) ctl->flag = static_cast<int>(atomicAdd(&a.ctr[1], 1u));
         if (!consumer_barrier(ctl)) return false;
-        const int h = *reinterpret_cast<volatile int*>(&ctl->flag);
+        const long long i = static_cast<unsigned int>(*reinterpret_cast<volatile int*>(&ctl->flag));
         // every thread has read the claim before thread 0 writes the next one
         if (!consumer_barrier(ctl)) return false;
-        if (h < 0 || h >= a.BH) break;
-        if (tid < D) combine_head<D>(a.peer, a.BH, h, tid, step, o);
-    }
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(&a.fold[1], 1u) == gridDim.x - 1) {
-            // every CTA has emitted, claimed and merged: the step is done here
-            atomicExch(&a.fold[0], 0u);
-            atomicExch(&a.fold[1], 0u);
-            a.peer.own[kHdrEpoch] = step;
+        if (i >= ncand) break;
+        long long head0;
+        if (by_head) {
+            head0 = i * a.S;
+        } else {
+            const long long row = (i + 1) * C;
+            if (row % a.S == 0) continue;  // the boundary falls between heads
+            head0 = row / a.S * a.S;
         }
+        const long long u_first = head0 / C;
+        const long long u_last = (head0 + a.S - 1) / C;
+        if (u_first == u_last) continue;   // a whole head, finished where it was streamed
+        if (!merge_cut_head<D, BS, kHalfKV, OUT>(a, merge, ctl, static_cast<int>(head0 / a.S),
+                                                 static_cast<int>(u_last - u_first + 1), tid))
+            return false;
+    }
+    return true;
+}
+
+// kOutExchange, after the merges: the CTA claims heads from ctr[2] and merges
+// every rank's records of each into O (combine_head), warp 0 first watching
+// each rank's m entry.  A head's entries come from every rank, this one
+// included, i.e. from CTAs of this launch that are past their own streaming
+// (merges of cut heads wait only as described at merge_epilogue), so all
+// waits end.  Across ranks nothing is circular: each rank emits all of its
+// records of the step before any of its CTAs waits for a peer.  `step` is the
+// step being completed.  Returns false when a consumer barrier gave up.
+template <int D>
+__device__ __forceinline__ bool exchange_epilogue(const DecodeArgs& a, CtaCtl* ctl, int tid,
+                                                  unsigned int& step) {
+    step = __ldcg(a.peer.own + kHdrEpoch) + 1u;
+    __half* o = static_cast<__half*>(a.out);
+    const long long stride = static_cast<long long>(a.BH) * (D + 2);
+    for (;;) {
+        if (tid == 0) ctl->flag = static_cast<int>(atomicAdd(&a.ctr[2], 1u));
+        if (!consumer_barrier(ctl)) return false;
+        const int h = *reinterpret_cast<volatile int*>(&ctl->flag);
+        if (!consumer_barrier(ctl)) return false;
+        if (h < 0 || h >= a.BH) break;
+        if (tid < 32) {
+            const unsigned long long* m0 = a.peer.own_recs +
+                (static_cast<long long>(step & 1u) * a.peer.world * a.BH + h) * (D + 2) + D;
+            lanes_wait_tagged(m0, stride, a.peer.world, step);
+        }
+        if (!consumer_barrier(ctl)) return false;
+        if (tid < D) combine_head<D>(a.peer, a.BH, h, tid, step, o);
     }
     return true;
 }
@@ -1180,7 +1230,6 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         }
         ctl->flag = 0;
         ctl->abort = 0u;
-        ctl->ndefer = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -1210,19 +1259,29 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         }
         const TileMeta m = meta[stage];
         if (m.flags & kTileDone) {
-            // the cut heads whose first piece this CTA streamed (list written
-            // by thread 0 before the last segment's closing barrier)
-            const int nd = *reinterpret_cast<volatile int*>(&ctl->ndefer);
-            const int2* defer = reinterpret_cast<const int2*>(reinterpret_cast<uint8_t*>(ctl) + 32);
-            for (int i = 0; i < nd; ++i) {
-                const int2 e = defer[i];
-                if (!merge_cut_head<D, BS, kHalfKV, OUT>(a, merge, ctl, e.x, e.y, tid)) {
+            if (a.ctr == nullptr) return;  // one CTA streamed everything: nothing was cut
+            if (a.nchunks > 1 && !merge_epilogue<D, BS, kHalfKV, OUT>(a, merge, ctl, tid)) {
+                consumer_leave(ctl);
+                return;
+            }
+            unsigned int step = 0;
+            if constexpr (OUT == kOutExchange) {
+                if (!exchange_epilogue<D>(a, ctl, tid, step)) {
                     consumer_leave(ctl);
                     return;
                 }
             }
-            if constexpr (OUT == kOutExchange) {
-                if (!exchange_epilogue<D>(a, ctl, tid)) consumer_leave(ctl);
+            // the last CTA to get here hands the counters back zeroed (every
+            // CTA has made its last claim) and, exchanging, completes the step
+            if (tid == 0) {
+                __threadfence();
+                if (atomicAdd(&a.ctr[3], 1u) == gridDim.x - 1) {
+                    atomicExch(&a.ctr[0], 0u);
+                    atomicExch(&a.ctr[1], 0u);
+                    atomicExch(&a.ctr[2], 0u);
+                    atomicExch(&a.ctr[3], 0u);
+                    if constexpr (OUT == kOutExchange) a.peer.own[kHdrEpoch] = step;
+                }
             }
             return;
         }
@@ -1297,6 +1356,12 @@ __global__ void __launch_bounds__(D)
     const int bh = blockIdx.x;
     const int t = threadIdx.x;
     const unsigned int step = __ldcg(p.own + kHdrEpoch) + 1u;
+    if (t < 32) {
+        const unsigned long long* m0 =
+            p.own_recs + (static_cast<long long>(step & 1u) * p.world * BH + bh) * (D + 2) + D;
+        lanes_wait_tagged(m0, static_cast<long long>(BH) * (D + 2), p.world, step);
+    }
+    __syncthreads();
     combine_head<D>(p, BH, bh, t, step, o);
     // the last CTA of the step advances this rank's step counter; every CTA
     // has read it above, before adding itself to the count

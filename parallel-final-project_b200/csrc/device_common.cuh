@@ -22,8 +22,6 @@ enum DeviceErrorCode : unsigned int {
     kErrDrainTimeout = 3,        // producer's copies never completed
     kErrPeerWaitTimeout = 4,     // a peer GPU's exchange entries never arrived
     kErrPieceWaitTimeout = 5,    // a piece of a head split across CTAs never arrived
-    kErrDeferOverflow = 6,       // more first pieces than a CTA can hold (cannot happen:
-                                 // the producer stops claiming chunks before that)
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {

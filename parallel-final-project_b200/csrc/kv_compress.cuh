@@ -12,8 +12,9 @@
 // fp16, one 8-byte store of codes); D/8 lanes cover a token row, so a warp
 // handles 32/(D/8) rows per step and the block max is a shuffle reduction
 // over BS/8 lanes.  A grid-stride loop over row groups replaces the
-// reference's one-CTA-per-row launch (16.7 M CTAs at S = 131072), with
-// kCompressUnroll row groups (their 16-byte loads) in flight per warp.
+// reference's one-CTA-per-row launch (16.7 M CTAs at S = 131072); the loop
+// is software-pipelined, so while a warp quantises kCompressUnroll row
+// groups the 16-byte loads of the next kCompressUnroll are in flight.
 #pragma once
 
 #include <cstdint>
@@ -164,22 +165,33 @@ __global__ void __launch_bounds__(kCompressThreads)
     const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
+    // Software-pipelined: the loads of the next row groups are issued before
+    // the current ones are quantised and stored, so 2 * kU 16-byte loads per
+    // lane are in flight while the warp computes.
     constexpr int kU = kCompressUnroll;
-    for (long long r0 = warp * (kU * kRPW); r0 < rows; r0 += nwarps * (kU * kRPW)) {
-        long long row[kU];
-        bool valid[kU];
-        uint4 raw[kU];
+    const long long step = nwarps * (kU * kRPW);
+    long long r0 = warp * (kU * kRPW);
+    uint4 raw[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+        const long long row = r0 + u * kRPW + rsub;
+        raw[u] = row < rows ? ld_stream_v4(x + row * kLPR + c) : make_uint4(0, 0, 0, 0);
+    }
+    for (; r0 < rows; r0 += step) {
+        uint4 nxt[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
-            row[u] = r0 + u * kRPW + rsub;
-            valid[u] = row[u] < rows;
-            raw[u] = make_uint4(0, 0, 0, 0);
-            if (valid[u]) raw[u] = ld_stream_v4(x + row[u] * kLPR + c);
+            const long long row = r0 + step + u * kRPW + rsub;
+            nxt[u] = row < rows ? ld_stream_v4(x + row * kLPR + c) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int u = 0; u < kU; ++u)
-            compress_lane<D, BS, MODE>(raw[u], append_row(row[u], T, S_cap, t0), valid[u], c, xq,
+        for (int u = 0; u < kU; ++u) {
+            const long long row = r0 + u * kRPW + rsub;
+            compress_lane<D, BS, MODE>(raw[u], append_row(row, T, S_cap, t0), row < rows, c, xq,
                                        scales);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) raw[u] = nxt[u];
     }
 }
 
@@ -202,18 +214,26 @@ __global__ void __launch_bounds__(kCompressThreads)
     const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
-    for (long long g0 = warp * (32 * kN); g0 < n8; g0 += nwarps * (32 * kN)) {
-        uint2 raw[kN];
-        __half sh[kN];
+    // Software-pipelined as Kernel A: the next step's groups are loaded before
+    // the current ones are converted and stored.
+    const long long step = nwarps * (32 * kN);
+    long long g0 = warp * (32 * kN);
+    uint2 raw[kN];
+    __half sh[kN];
+#pragma unroll
+    for (int u = 0; u < kN; ++u) {
+        const long long g = g0 + u * 32 + lane;
+        raw[u] = g < n8 ? ld_stream_v2(xq + g) : make_uint2(0u, 0u);
+        sh[u] = g < n8 ? scales[(g * 8) / BS] : __ushort_as_half(0);
+    }
+    for (; g0 < n8; g0 += step) {
+        uint2 nraw[kN];
+        __half nsh[kN];
 #pragma unroll
         for (int u = 0; u < kN; ++u) {
-            const long long g = g0 + u * 32 + lane;
-            raw[u] = make_uint2(0u, 0u);
-            sh[u] = __ushort_as_half(0);
-            if (g < n8) {
-                raw[u] = ld_stream_v2(xq + g);
-                sh[u] = scales[(g * 8) / BS];
-            }
+            const long long g = g0 + step + u * 32 + lane;
+            nraw[u] = g < n8 ? ld_stream_v2(xq + g) : make_uint2(0u, 0u);
+            nsh[u] = g < n8 ? scales[(g * 8) / BS] : __ushort_as_half(0);
         }
 #pragma unroll
         for (int u = 0; u < kN; ++u) {
@@ -234,6 +254,11 @@ __global__ void __launch_bounds__(kCompressThreads)
                 }
             }
             st_stream_v4(y + g, make_uint4(out[0], out[1], out[2], out[3]));
+        }
+#pragma unroll
+        for (int u = 0; u < kN; ++u) {
+            raw[u] = nraw[u];
+            sh[u] = nsh[u];
         }
     }
 }

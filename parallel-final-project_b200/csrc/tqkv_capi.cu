@@ -42,15 +42,13 @@ thread_local int t_last_cuda_error = 0;
 
 constexpr long long kMinRowsPerCta = 256;  // below this a CTA is mostly pipeline fill
 constexpr long long kChunksPerCta = 8;     // scheduling chunks per CTA (load balance)
-// A CTA claims at most kMaxDefer chunks; the plan's kChunksPerCta per CTA on
-// average leaves room for CTAs that stream four times faster than the rest.
-static_assert(4 * kChunksPerCta <= kMaxDefer, "chunk claims per CTA");
 constexpr long long kChunkAlign = 128;     // chunk rows: a multiple of every tile height
-// Below this many rows per CTA every CTA takes one run of rows, statically:
-// each chunk boundary costs a head piece (a record, a ticket and consumer
-// barriers), which short chunks cannot amortise.  Measured on one B200 with
-// 592 CTAs: dynamic chunks win 1.4 % at 28k rows per CTA (long-context
-// decode), and lose 14 % at 7k rows per CTA (B16 H32 S8192).
+// Below this many rows per CTA the rows are cut into one chunk per CTA:
+// every chunk boundary inside a head costs a head piece (a record, consumer
+// barriers, a share of the head's merge), which short chunks cannot
+// amortise.  Measured on one B200 with 592 CTAs: ~8 chunks per CTA win 1.4 %
+// at 28k rows per CTA (long-context decode), and lose 14 % at 7k rows per
+// CTA (B16 H32 S8192).
 constexpr long long kMinDynamicRowsPerCta = 16384;
 constexpr int kMaxCtasPerSmBound = 4;      // >= any decode kernel's occupancy (smem-bound)
 
@@ -104,12 +102,12 @@ struct DecodePlan {
     int max_parts;
 };
 
-// The B*H*S rows, heads laid end to end, are cut into fixed chunks of C rows.
-// Normally there is one chunk per CTA (C = rows / grid, rounded to 16): equal
-// work for every CTA and the fewest head pieces.  When a CTA would stream at
-// least kMinDynamicRowsPerCta rows, C is cut to about 1/kChunksPerCta of that
-// (a multiple of 128) and the CTAs claim chunks dynamically, so SMs that
-// stream faster take more of them; each chunk is then long enough (>= 32
+// The B*H*S rows, heads laid end to end, are cut into fixed chunks of C rows,
+// which the CTAs claim from a counter.  Normally there is one chunk per CTA
+// (C = rows / grid, rounded to 16): equal work for every CTA and the fewest
+// head pieces.  When a CTA would stream at least kMinDynamicRowsPerCta rows,
+// C is cut to about 1/kChunksPerCta of that (a multiple of 128), so SMs that
+// stream faster take more chunks; each chunk is then long enough (>= 32
 // tiles) to amortise the extra head pieces it creates.  `max_ctas` caps the
 // grid (resident CTAs).
 DecodePlan make_plan(long long BH, int S, long long max_ctas) {
@@ -147,9 +145,9 @@ DecodePlan bound_plan(long long BH, int S, int device) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// [0, 16): counters (chunk scheduler: next chunk, producers done; exchange
-// epilogue: heads claimed, CTAs done); from 256: max_parts tagged records of
-// D + 2 64-bit values per head.  All zero between calls.
+// [0, 16): counters (next chunk, cut heads claimed for merging, heads
+// claimed for the exchange merge, CTAs finished); from 256: max_parts tagged
+// records of D + 2 64-bit values per head.  All zero between calls.
 struct WsLayout {
     size_t sched_off, parts_off, total;
 };
@@ -181,31 +179,6 @@ cudaError_t launch_kernel(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t sm
         ((ptrs[i++] = static_cast<void*>(&v)), ...);
     }, vals);
     return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, block, ptrs, smem, stream);
-}
-
-// Cooperative launch (every CTA of the grid resident at once), for kernels
-// whose CTAs wait on one another.  Same error behaviour as launch_kernel.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_kernel_coop(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                               cudaStream_t stream, Args... args) {
-    static_assert(sizeof...(KArgs) == sizeof...(Args), "argument count");
-    std::tuple<KArgs...> vals(static_cast<KArgs>(args)...);
-    void* ptrs[sizeof...(KArgs) > 0 ? sizeof...(KArgs) : 1];
-    std::apply([&](auto&... v) {
-        int i = 0;
-        ((ptrs[i++] = static_cast<void*>(&v)), ...);
-    }, vals);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(fn), ptrs);
 }
 
 template <int D, int BS>
@@ -276,9 +249,9 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     if (needs_ws && (workspace == nullptr || workspace_bytes < lay.total)) return TQKV_ERR_WORKSPACE;
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    // one chunk per CTA: no claims, chunk = blockIdx.x
-    a.sched = plan.nchunks > plan.grid ? reinterpret_cast<unsigned int*>(ws + lay.sched_off)
-                                        : nullptr;
+    // chunk claims, merge and exchange claims, CTAs finished; without a
+    // workspace one CTA streams the single chunk
+    a.ctr = needs_ws ? reinterpret_cast<unsigned int*>(ws + lay.sched_off) : nullptr;
     a.recs = needs_ws ? reinterpret_cast<unsigned long long*>(ws + lay.parts_off) : nullptr;
     a.total_rows = static_cast<long long>(BH) * S;
     a.chunk_rows = plan.chunk_rows;
@@ -287,13 +260,8 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     a.BH = BH;
     a.max_parts = bound.max_parts;
     a.score_scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
-    // counters [2], [3] of the scheduler area
-    if constexpr (kFold) a.fold = reinterpret_cast<unsigned int*>(ws + lay.sched_off) + 2;
-    // Cooperative: a CTA may wait for the records of pieces that other CTAs
-    // stream (and, exchanging, merge), so every CTA must be resident; the
-    // plan's grid never exceeds the resident CTAs.
-    return from_cuda(launch_kernel_coop(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
-                                        stream, a));
+    return from_cuda(launch_kernel(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
+                                   stream, a));
 }
 
 template <int D, int BS, bool kHalfKV>

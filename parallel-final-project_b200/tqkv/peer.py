@@ -11,7 +11,7 @@ into every other rank's buffer.  Per decode step:
     combine(out)   bounded wait until this rank's buffer holds every rank's
                    entries of this step, merge into O, advance the step
 
-or both in one cooperative launch, step(..., out) (step_append with the
+or both in one launch, step(..., out) (step_append with the
 newest tokens appended): after its share of the slice, each CTA of the decode
 launch merges heads whose records have arrived from every rank, so the
 exchange overlaps the other CTAs' streaming and no second launch is needed.

@@ -93,7 +93,6 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0, group=1)
         r0, r1 = c * R, min((c + 1) * R, total)
         assert r0 < r1
         r = r0
-        firsts = 0
         while r < r1:
             bh = r // S
             head0 = bh * S
@@ -144,15 +143,17 @@ def check(BH, S, D, bs, half, occ, offs=(0, 0), S_stride=None, T_new=0, group=1)
                     assert (qsrc & 15) + D * 2 <= qslot
             c_first, c_last = head0 // R, (head0 + S - 1) // R
             assert 0 <= c - c_first < c_last - c_first + 1 <= maxp
-            if c == c_first and c_last > c_first:   # the first piece of a cut head:
-                firsts += 1                         # merged at the end of its CTA
             covered += tb - ta
             r = head0 + tb
-        # each chunk leaves its CTA at most one cut head to merge, and a CTA
-        # claims at most kMaxDefer chunks, which covers every chunk
-        assert firsts <= 1
-    assert nchunks <= grid * _const("decode_attn.cuh", "kMaxDefer") // 4
     assert covered == total
+    # the merge claims: every cut head is a candidate exactly once
+    cut = {h for h in range(BH) if (h * S) // R != (h * S + S - 1) // R}
+    if R <= S:
+        cands = [h for h in range(BH) if (h * S) // R != (h * S + S - 1) // R]
+    else:
+        cands = [(i + 1) * R // S for i in range(nchunks - 1) if ((i + 1) * R) % S]
+        cands = [h for h in cands if (h * S) // R != (h * S + S - 1) // R]
+    assert sorted(cands) == sorted(cut) and len(cands) == len(set(cands))
 
 
 KINDS = [(64, 32, False), (64, 64, False), (128, 32, False), (128, 64, False), (128, 128, False),
@@ -180,15 +181,14 @@ def test_schedule_in_bounds_with_cache_stride(D, bs):
 
 def test_stage_layout_fits_four_ctas_per_sm():
     """3-stage ring + merge scratch + barriers + tile descriptors + control
-    block + list of cut heads to merge, of the largest instantiation (INT8,
-    D = 128, bs = 32), leave room for four CTAs in 228 KB."""
+    block of the largest instantiation (INT8, D = 128, bs = 32) leave room
+    for four CTAs in 228 KB."""
     RB, nsub, D = 128, 4, 128
     TILE = TILE_BYTES // RB
-    defer = _const("decode_attn.cuh", "kMaxDefer")
     stage = 2 * TILE_BYTES + 2 * (TILE * nsub * 2 + 32) + (D * 2 + 32)
     slices = WARPS * 32 // (D // 4)
     merge = -(-max(WARPS * (D + 2), slices * (D + 4)) * 4 // 16) * 16
-    smem = STAGES * stage + merge + 2 * STAGES * 8 + STAGES * 32 + 32 + defer * 8
+    smem = STAGES * stage + merge + 2 * STAGES * 8 + STAGES * 32 + 32
     assert 4 * (smem + 1024) <= 228 * 1024, smem
 
 
@@ -261,14 +261,13 @@ def test_exchange_buffer_holds_every_entry():
     assert lib.tqkv_exchange_bytes(2, 4, 96) == 0
 
 
-def test_exchange_merge_counters_fit_the_scheduler_area():
-    """The one-launch exchange keeps its two merge counters (heads claimed,
-    CTAs finished) after the two chunk-scheduler counters, before the
-    records of the pieces of cut heads (which start on 16 bytes)."""
-    src = open(os.path.join(CSRC, "tqkv_capi.cu")).read()
-    m = re.search(r"a\.fold = reinterpret_cast<unsigned int\*>\(ws \+ lay\.sched_off\) \+ (\d+);", src)
-    assert m, "fold counter placement"
-    first = int(m.group(1))
-    recs = re.search(r"w\.parts_off = (\d+);", src)
-    assert recs
-    assert first >= 2 and 4 * (first + 2) <= int(recs.group(1)) and int(recs.group(1)) % 16 == 0
+def test_workspace_counters_fit_before_the_records():
+    """The four workspace counters (next chunk, cut heads claimed, exchange
+    heads claimed, CTAs finished: ctr[0..3]) lie before the records of the
+    pieces of cut heads, which start on 16 bytes."""
+    src = open(os.path.join(CSRC, "decode_attn.cuh")).read()
+    used = {int(i) for i in re.findall(r"a\.ctr\[(\d+)\]", src)}
+    assert used == {0, 1, 2, 3}, used
+    capi = open(os.path.join(CSRC, "tqkv_capi.cu")).read()
+    recs = re.search(r"w\.parts_off = (\d+);", capi)
+    assert recs and 4 * (max(used) + 1) <= int(recs.group(1)) and int(recs.group(1)) % 16 == 0

@@ -1,6 +1,6 @@
 """The split-S exchange step on one GPU: the one-launch form
 (tqkv_decode_int8_exchange: decode, record exchange and merge in one
-cooperative launch) against the two-launch form (publish + combine) and the
+launch) against the two-launch form (publish + combine) and the
 plain decode; ranks whose token slice is empty; and the bounded waits for
 peer records running out.
 

@@ -65,7 +65,7 @@ def _rank_main(rank, world, port, q_out):
                 if step % 2 == 0:      # two launches: publish, then combine
                     ex.publish(qs, kq, ks, vq, vs, w.block_size)
                     o2 = ex.combine(torch.empty_like(o))
-                else:                  # one cooperative launch
+                else:                  # one launch
                     o2 = ex.step(qs, kq, ks, vq, vs, w.block_size, torch.empty_like(o))
                 ref2 = tqkv.decode_int8(qs, kqf, ksf, vqf, vsf, w.block_size)
                 torch.cuda.synchronize()
