@@ -618,6 +618,12 @@ def main():
     # between it and the timed steps: every rank's combine ends only once all
     # ranks have published that step, so whatever host skew the ranks leave
     # the barrier with is absorbed there and the timed regions start together.
+    # With one launch per step and no L2 overwrite, nothing but the steps runs
+    # in the timed region: its time / K is both the step and the launch time,
+    # and per-step events (a few us of their own per step) stay out of it;
+    # per-step samples come from a second pass below.
+    single_launch = not (collective and not one_launch)
+    per_step_events = flush_buf is not None or not single_launch
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
            for _ in range(args.steps)]
     with ClockSampler(local) as clk:
@@ -631,11 +637,14 @@ def main():
         for i in range(args.steps):
             if flush_buf is not None:
                 flush_buf.zero_()
-            kev[i][0].record()
+            if per_step_events:
+                kev[i][0].record()
             run_kernel()
-            kev[i][1].record()
+            if per_step_events:
+                kev[i][1].record()
             run_comm()
-            kev[i][2].record()
+            if per_step_events:
+                kev[i][2].record()
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -645,7 +654,23 @@ def main():
         step_ms_local = ev0.elapsed_time(ev1) / args.steps
     else:
         step_ms_local = statistics.mean(a.elapsed_time(c) for a, _, c in kev)
-    kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    if per_step_events:
+        kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    else:
+        kern_ms_local = step_ms_local
+        # per-step samples: the same K steps again, each bracketed by events
+        torch.cuda.synchronize()
+        barrier()
+        run_kernel()
+        run_comm()
+        for i in range(args.steps):
+            kev[i][0].record()
+            run_kernel()
+            kev[i][1].record()
+            run_comm()
+            kev[i][2].record()
+        torch.cuda.synchronize()
+        barrier()
     step_samples_ms = [a.elapsed_time(c) for a, _, c in kev]   # per step, this rank
     # step-to-step period (start of one step to the start of the next)
     period_ms_local = (statistics.median(kev[i][0].elapsed_time(kev[i + 1][0])
@@ -765,6 +790,9 @@ def main():
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": peak_kind, "traffic": traffic,
             "algorithmic_bytes_per_launch": local_bytes, "launch_ms": kern_ms,
+            "launch_timing": ("timed region / K: one launch per step, back to back"
+                              if not per_step_events else
+                              "mean of per-launch CUDA events inside the timed region"),
         },
         "cpu_baseline": cpu,
         "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",

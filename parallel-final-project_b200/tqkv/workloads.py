@@ -66,6 +66,10 @@ WORKLOADS = {
         "int8_gpt2_outlier", 8, 12, 1024, 64, 64, 3, "outlier_channels",
         "INT8 decode B8 H12 D64 S1024 bs64, K/V ~ N(0,1) with ceil(1% of D) channel per head "
         "x10, V + per-(h,d) N(0,0.1) bias, seed 3"),
+    "int8_longctx_s16k": Workload(
+        "int8_longctx_s16k", 4, 32, 16384, 128, 128, 4, "normal",
+        "INT8 decode B4 H32 D128 S16384 bs128, K/V ~ N(0,1), seed 4: one GPU's token slice of "
+        "the long-context configuration at 8 GPUs (its first 16384 tokens)"),
     "int8_longctx": Workload(
         "int8_longctx", 4, 32, 131072, 128, 128, 4, "normal",
         "INT8 long-context decode B4 H32 D128 S131072 bs128, K/V ~ N(0,1), seed 4; "
