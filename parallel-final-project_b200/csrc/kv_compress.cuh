@@ -55,6 +55,42 @@ __device__ __forceinline__ float kv_div(float a, float b) {
     return r;
 }
 
+// x / b for many x and one b.  The approximate forms are defined as
+// x * (1 / b) (PTX ISA, div.approx), so the reciprocal is taken once and each
+// quotient is one multiply, with the same flush-to-zero behaviour; the
+// correctly rounded forms divide each x.
+template <int MODE>
+struct KvQuotient {
+    float b, r;
+    __device__ __forceinline__ explicit KvQuotient(float b_) : b(b_), r(0.0f) {
+        if constexpr (MODE == kDivApproxFtz) {
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(b));
+        } else if constexpr (MODE == kDivApprox) {
+            asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(b));
+        }
+    }
+    __device__ __forceinline__ float operator()(float x) const {
+        float q;
+        if constexpr (MODE == kDivApproxFtz) {
+            asm("mul.ftz.f32 %0, %1, %2;" : "=f"(q) : "f"(x), "f"(r));
+        } else if constexpr (MODE == kDivApprox) {
+            asm("mul.f32 %0, %1, %2;" : "=f"(q) : "f"(x), "f"(r));
+        } else {
+            q = kv_div<MODE>(x, b);
+        }
+        return q;
+    }
+};
+
+// round-to-nearest-even of x as a signed byte, saturated to [-128, 127], NaN
+// to 0, in the low byte of the result (PTX lets cvt write a narrow integer
+// type into a 32-bit register)
+__device__ __forceinline__ uint32_t cvt_rni_sat_s8(float x) {
+    uint32_t v;
+    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(v) : "f"(x));
+    return v;
+}
+
 constexpr int kCompressThreads = 256;
 constexpr int kCompressUnroll = 4;  // row groups whose loads a warp keeps in flight
 
@@ -110,21 +146,22 @@ __device__ __forceinline__ uint2 quantize_lane(uint4 raw, __half& scale) {
     float s = kv_div<MODE>(a, 127.0f);
     if (s == 0.0f) s = 1.0f;
     scale = __float2half_rn(s);
+    const KvQuotient<MODE> by_s(s);  // x / s for the lane's 8 values
 
-    uint32_t packed[2];
+    // code = clamp(round_half_even(x / s), -127, 127), NaN -> 0, as one
+    // saturating conversion per value.  Its range is [-128, 127], and the
+    // bound -127 is never reached from below: |x| <= m, so in every division
+    // mode |x / s| <= 127 * (1 + 1e-6) < 127.5.  An x that is NaN, or +-inf
+    // (then s = inf and x / s is NaN), converts to 0.  The codes are packed
+    // by byte permutes from the low bytes of the conversions.
+    uint32_t c[8];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            int qi = __float2int_rn(kv_div<MODE>(f[4 * h + b], s));
-            qi = qi > 127 ? 127 : qi;
-            qi = qi < -127 ? -127 : qi;
-            word |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * b);
-        }
-        packed[h] = word;
-    }
-    return make_uint2(packed[0], packed[1]);
+    for (int i = 0; i < 8; ++i) c[i] = cvt_rni_sat_s8(by_s(f[i]));
+    const uint32_t lo = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040),
+                                    0x5410);
+    const uint32_t hi = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040),
+                                    0x5410);
+    return make_uint2(lo, hi);
 }
 
 // Quantise lane c's 8 values of a row and store its codes and, on the first
@@ -144,16 +181,21 @@ __device__ __forceinline__ void compress_lane(uint4 raw, long long row, bool val
 }
 
 // Destination row of source row `r` when T rows per head are written at rows
-// [t0, t0 + T) of a cache holding S_cap rows per head (identity when T == S_cap).
+// [t0, t0 + T) of a cache holding S_cap rows per head (identity for whole
+// tensors, APPEND false).
+template <bool APPEND>
 __device__ __forceinline__ long long append_row(long long r, int T, int S_cap, int t0) {
-    if (T == S_cap) return r;
-    const long long bh = r / T;
-    return bh * S_cap + t0 + (r - bh * T);
+    if constexpr (!APPEND) {
+        return r;
+    } else {
+        const long long bh = r / T;
+        return bh * S_cap + t0 + (r - bh * T);
+    }
 }
 
 // x: fp16 rows as uint4 (8 halves each), xq: codes as uint2 (8 bytes each).
 // Source rows are [B*H*T]; see append_row for where they land.
-template <int D, int BS, int MODE>
+template <int D, int BS, int MODE, bool APPEND>
 __global__ void __launch_bounds__(kCompressThreads)
     kv_compress_kernel(const uint4* __restrict__ x, uint2* __restrict__ xq,
                        __half* __restrict__ scales, long long rows, int T, int S_cap, int t0) {
@@ -167,10 +209,13 @@ __global__ void __launch_bounds__(kCompressThreads)
 
     // Software-pipelined: the loads of the next row groups are issued before
     // the current ones are quantised and stored, so 2 * kU 16-byte loads per
-    // lane are in flight while the warp computes.
+    // lane are in flight while the warp computes.  A step whose next row
+    // groups all lie below `rows` (every step but a warp's last one or two)
+    // runs without per-row bounds checks; the test is warp-uniform.
     constexpr int kU = kCompressUnroll;
-    const long long step = nwarps * (kU * kRPW);
-    long long r0 = warp * (kU * kRPW);
+    constexpr int kRowsPerStep = kU * kRPW;
+    const long long step = nwarps * kRowsPerStep;
+    long long r0 = warp * kRowsPerStep;
     uint4 raw[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -179,16 +224,28 @@ __global__ void __launch_bounds__(kCompressThreads)
     }
     for (; r0 < rows; r0 += step) {
         uint4 nxt[kU];
+        if (r0 + step + kRowsPerStep <= rows) {
+            const uint4* src = x + (r0 + step + rsub) * kLPR + c;
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const long long row = r0 + step + u * kRPW + rsub;
-            nxt[u] = row < rows ? ld_stream_v4(x + row * kLPR + c) : make_uint4(0, 0, 0, 0);
-        }
+            for (int u = 0; u < kU; ++u) nxt[u] = ld_stream_v4(src + u * kRPW * kLPR);
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const long long row = r0 + u * kRPW + rsub;
-            compress_lane<D, BS, MODE>(raw[u], append_row(row, T, S_cap, t0), row < rows, c, xq,
-                                       scales);
+            for (int u = 0; u < kU; ++u) {
+                const long long row = r0 + u * kRPW + rsub;
+                compress_lane<D, BS, MODE>(raw[u], append_row<APPEND>(row, T, S_cap, t0), true, c,
+                                           xq, scales);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const long long row = r0 + step + u * kRPW + rsub;
+                nxt[u] = row < rows ? ld_stream_v4(x + row * kLPR + c) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const long long row = r0 + u * kRPW + rsub;
+                compress_lane<D, BS, MODE>(raw[u], append_row<APPEND>(row, T, S_cap, t0),
+                                           row < rows, c, xq, scales);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kU; ++u) raw[u] = nxt[u];

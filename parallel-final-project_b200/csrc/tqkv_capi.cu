@@ -187,7 +187,8 @@ tqkv_status compress_impl(const void* x, int8_t* xq, void* scales, long long row
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return from_cuda(e);
-    auto fn = kv_compress_kernel<D, BS, TQKV_COMPRESS_DIV_MODE>;
+    auto fn = T == S_cap ? kv_compress_kernel<D, BS, TQKV_COMPRESS_DIV_MODE, false>
+                         : kv_compress_kernel<D, BS, TQKV_COMPRESS_DIV_MODE, true>;
     const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
     const long long rows_per_block =
         static_cast<long long>(kCompressUnroll) * (kCompressThreads / 32) * (32 / (D / 8));
