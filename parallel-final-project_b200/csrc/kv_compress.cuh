@@ -93,6 +93,12 @@ __device__ __forceinline__ uint32_t cvt_rni_sat_s8(float x) {
 
 constexpr int kCompressThreads = 256;
 constexpr int kCompressUnroll = 4;  // row groups whose loads a warp keeps in flight
+// 8-code groups whose loads a Kernel B lane keeps in flight.  Kernel B runs
+// one 256-thread CTA per SM (about 150 registers a thread); on B200 that
+// streams faster than 8 groups a lane at 2 to 4 CTAs per SM, or 12 or 24
+// groups a lane (B4 H32 S131072 D128: 1.03 ms against 1.07 to 1.16 ms per
+// 6.5 GB tensor).
+constexpr int kReconstructInFlight = 16;
 
 __device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
     uint4 v;
@@ -252,19 +258,47 @@ __global__ void __launch_bounds__(kCompressThreads)
     }
 }
 
-// Kernel B: y = fp16(float(code) * float(scale)).  The product of a 7-bit
-// code and an 11-bit scale is exact in fp32, so the only rounding is the
-// final fp16 conversion, as in the reference (src/kv_reconstruct.cu:33).
+// Kernel B: y = fp16(float(code) * float(scale)).  The product of a code
+// (at most 8 bits) and an fp16 scale (11 significant bits) is exact in fp32,
+// so the reference's only rounding is the final fp16 conversion
+// (src/kv_reconstruct.cu:33).  The same value comes out of fp16x2 arithmetic
+// with no conversions at all:
+//   * the code c becomes the fp16 value 1024 + (c + 128) by placing the byte
+//     c ^ 0x80 under the exponent byte 0x64 (a byte permute), and subtracting
+//     1152 leaves c exactly;
+//   * one fp16x2 multiply, round-to-nearest-even with subnormals kept, rounds
+//     the exact product c * scale once, as the conversion of the exact fp32
+//     product does (overflow to inf, NaN, signed zeros included).
 // The codes are taken as a flat run of 8-code groups (8 divides BS and D, so
 // a group never straddles a scale block): lane l of a warp instruction reads
 // group g0 + l (8 bytes) and writes its 8 halves (16 bytes), so every load
 // covers 256 contiguous bytes and every store 512.  Each warp step issues
-// 2 * kCompressUnroll such loads per lane before converting any of them.
+// kReconstructInFlight such loads per lane before converting any of them.
+__device__ __forceinline__ uint4 reconstruct_group(uint2 codes, __half scale) {
+    const __half2 s2 = __half2half2(scale);
+    const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152
+    const uint32_t w[2] = {codes.x ^ 0x80808080u, codes.y ^ 0x80808080u};
+    uint32_t out[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            // bytes (low to high): code 2p, 0x64, code 2p+1, 0x64
+            const uint32_t biased = __byte_perm(w[i], 0x64646464u, p == 0 ? 0x4140 : 0x4342);
+            const __half2 c = __hsub2_rn(*reinterpret_cast<const __half2*>(&biased), bias);
+            const __half2 y = __hmul2_rn(c, s2);
+            out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&y);
+        }
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 template <int D, int BS>
 __global__ void __launch_bounds__(kCompressThreads)
     kv_reconstruct_kernel(const uint2* __restrict__ xq, const __half* __restrict__ scales,
                           uint4* __restrict__ y, long long rows) {
-    constexpr int kN = 2 * kCompressUnroll;  // group loads in flight per lane
+    constexpr int kN = kReconstructInFlight;  // group loads in flight per lane
+    constexpr int kGroupsPerStep = 32 * kN;
     static_assert(BS % 8 == 0 && D % BS == 0, "8-code groups inside scale blocks");
     const long long n8 = rows * (D / 8);
     const int lane = threadIdx.x & 31;
@@ -272,9 +306,10 @@ __global__ void __launch_bounds__(kCompressThreads)
     const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
 
     // Software-pipelined as Kernel A: the next step's groups are loaded before
-    // the current ones are converted and stored.
-    const long long step = nwarps * (32 * kN);
-    long long g0 = warp * (32 * kN);
+    // the current ones are converted and stored; a step whose next groups all
+    // lie below n8 runs without per-group bounds checks (warp-uniform test).
+    const long long step = nwarps * kGroupsPerStep;
+    long long g0 = warp * kGroupsPerStep;
     uint2 raw[kN];
     __half sh[kN];
 #pragma unroll
@@ -286,31 +321,28 @@ __global__ void __launch_bounds__(kCompressThreads)
     for (; g0 < n8; g0 += step) {
         uint2 nraw[kN];
         __half nsh[kN];
+        if (g0 + step + kGroupsPerStep <= n8) {
+            const long long gn = g0 + step + lane;
 #pragma unroll
-        for (int u = 0; u < kN; ++u) {
-            const long long g = g0 + step + u * 32 + lane;
-            nraw[u] = g < n8 ? ld_stream_v2(xq + g) : make_uint2(0u, 0u);
-            nsh[u] = g < n8 ? scales[(g * 8) / BS] : __ushort_as_half(0);
-        }
-#pragma unroll
-        for (int u = 0; u < kN; ++u) {
-            const long long g = g0 + u * 32 + lane;
-            if (g >= n8) continue;
-            const float s = __half2float(sh[u]);
-            const uint32_t w[2] = {raw[u].x, raw[u].y};
-            uint32_t out[4];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-#pragma unroll
-                for (int p = 0; p < 2; ++p) {
-                    const int lo = static_cast<int8_t>((w[i] >> (16 * p)) & 0xffu);
-                    const int hi = static_cast<int8_t>((w[i] >> (16 * p + 8)) & 0xffu);
-                    const __half2 h = __halves2half2(__float2half_rn(static_cast<float>(lo) * s),
-                                                     __float2half_rn(static_cast<float>(hi) * s));
-                    out[2 * i + p] = *reinterpret_cast<const uint32_t*>(&h);
-                }
+            for (int u = 0; u < kN; ++u) {
+                nraw[u] = ld_stream_v2(xq + gn + u * 32);
+                nsh[u] = scales[((gn + u * 32) * 8) / BS];
             }
-            st_stream_v4(y + g, make_uint4(out[0], out[1], out[2], out[3]));
+#pragma unroll
+            for (int u = 0; u < kN; ++u)
+                st_stream_v4(y + g0 + u * 32 + lane, reconstruct_group(raw[u], sh[u]));
+        } else {
+#pragma unroll
+            for (int u = 0; u < kN; ++u) {
+                const long long g = g0 + step + u * 32 + lane;
+                nraw[u] = g < n8 ? ld_stream_v2(xq + g) : make_uint2(0u, 0u);
+                nsh[u] = g < n8 ? scales[(g * 8) / BS] : __ushort_as_half(0);
+            }
+#pragma unroll
+            for (int u = 0; u < kN; ++u) {
+                const long long g = g0 + u * 32 + lane;
+                if (g < n8) st_stream_v4(y + g, reconstruct_group(raw[u], sh[u]));
+            }
         }
 #pragma unroll
         for (int u = 0; u < kN; ++u) {

@@ -210,8 +210,8 @@ tqkv_status reconstruct_impl(const int8_t* xq, const void* scales, void* y, long
     if (e != cudaSuccess) return from_cuda(e);
     auto fn = kv_reconstruct_kernel<D, BS>;
     const int per_sm = prepare_kernel(fn, kCompressThreads, 0, dev);
-    // one warp step covers 32 * 2 * kCompressUnroll groups of 8 codes
-    const long long groups_per_block = (kCompressThreads / 32) * 32 * 2 * kCompressUnroll;
+    // one warp step covers 32 * kReconstructInFlight groups of 8 codes
+    const long long groups_per_block = (kCompressThreads / 32) * 32 * kReconstructInFlight;
     long long grid = (rows * (D / 8) + groups_per_block - 1) / groups_per_block;
     const long long cap = static_cast<long long>(sm_count(dev)) * (per_sm > 0 ? per_sm : 1);
     if (grid > cap) grid = cap;

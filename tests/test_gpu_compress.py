@@ -172,6 +172,34 @@ def test_reconstruct_bit_exact(D, bs, S):
     assert np.array_equal(to_np(y).view(np.uint16), yo.view(np.uint16))
 
 
+def test_reconstruct_exhaustive_codes_and_scales():
+    """Every code (all 256 bytes) times every fp16 scale bit pattern (65,536,
+    subnormals, infinities and NaNs included): bit-identical to the reference
+    build's Kernel B, and to the oracle wherever the oracle's result is not a
+    NaN (there the kernel must give a NaN too; the NaN payload is the GPU's)."""
+    rows = 65536 * 2
+    codes = (torch.arange(256, dtype=torch.int32, device="cuda").to(torch.uint8)
+             .view(torch.int8).repeat(65536).reshape(1, 1, rows, 128))
+    scales = (torch.arange(65536, dtype=torch.int32, device="cuda").to(torch.int16)
+              .repeat_interleave(2).view(torch.half).reshape(1, 1, rows, 1))
+    y = tqkv.kv_reconstruct(codes, scales, 128)
+    torch.cuda.synchronize()
+    yb = to_np(y).view(np.uint16)
+    yo = O.kv_reconstruct(to_np(codes), to_np(scales), 128).view(np.uint16)
+    nan_o = (yo & 0x7c00) == 0x7c00
+    nan_o &= (yo & 0x03ff) != 0
+    nan_g = ((yb & 0x7c00) == 0x7c00) & ((yb & 0x03ff) != 0)
+    assert np.array_equal(nan_g, nan_o)
+    assert np.array_equal(yb[~nan_o], yo[~nan_o])
+    if os.path.exists(REF_LIB):
+        lib = _ref_lib()
+        yr = torch.empty_like(y)
+        lib.ref_kv_reconstruct(codes.data_ptr(), scales.data_ptr(), yr.data_ptr(), 1, 1, rows,
+                               128, 128, _stream())
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), yr.view(torch.int16))
+
+
 def test_roundtrip_bound_full_longctx():
     """Size-independent property on the largest configuration: every
     element's round-trip error |x - code*scale| is at most half a scale step
