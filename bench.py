@@ -586,6 +586,7 @@ def main():
     # CUDA graphs: one for the decode kernel, one for gather + combine, one for
     # the whole end-to-end step; replays keep the GPU fed without launch gaps.
     graphs = []
+    steps_graph = None
     # NCCL collectives are never captured (capturing them hung here); the p2p
     # exchange is two plain kernels and captures like the single-GPU step.
     if not args.no_graph and not (collective and not use_p2p):
@@ -626,6 +627,19 @@ def main():
         if n_sets > 1:
             run_kernel = replay_next
         run_kernel_hot = set_graphs[0].replay
+        # With one launch per step, the timed steps are one graph of K launches,
+        # as a decoder that captures its decode loop runs them: consecutive
+        # launches then start ~2 us apart, where replaying one graph per step
+        # leaves 3-8 us between them.  Step i streams copy (1 + i) % n_sets; the
+        # aligning step before it streams copy 0.
+        if not two_part:
+            steps_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(steps_graph):
+                for i in range(args.steps):
+                    set_idx[0] = (1 + i) % n_sets
+                    kernel()
+            set_idx[0] = 0
+            graphs.append(steps_graph)
     else:
         turn = [0]
 
@@ -637,6 +651,8 @@ def main():
         run_kernel, run_comm, run_e2e = (eager_next if n_sets > 1 else kernel), comm, e2e_step
         run_kernel_hot = kernel
     graphs_used = len(graphs) > 0
+    if steps_graph is not None:
+        steps_graph.replay()          # warm-up of the graph itself
     for _ in range(args.warmup):
         run_kernel()
         run_comm()
@@ -663,19 +679,22 @@ def main():
         barrier()
         torch.cuda.synchronize()
         clk.mark_start()
-        run_kernel()
+        (run_kernel_hot if steps_graph is not None else run_kernel)()
         run_comm()
         torch.cuda.nvtx.range_push("tqkv_timed")  # lets ncu --nvtx-include select this region
         ev0.record()
-        for i in range(args.steps):
-            if per_step_events:
-                kev[i][0].record()
-            run_kernel()
-            if per_step_events:
-                kev[i][1].record()
-            run_comm()
-            if per_step_events:
-                kev[i][2].record()
+        if steps_graph is not None:
+            steps_graph.replay()
+        else:
+            for i in range(args.steps):
+                if per_step_events:
+                    kev[i][0].record()
+                run_kernel()
+                if per_step_events:
+                    kev[i][1].record()
+                run_comm()
+                if per_step_events:
+                    kev[i][2].record()
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -737,7 +756,25 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e2e_ms_local = ev0.elapsed_time(ev1) / e2e_steps
-    del graphs, run_kernel, run_comm, run_e2e
+
+    # the timed steps again as one graph replay per step (no per-step events),
+    # after the end-to-end steps so that they run in the same state as before
+    graph_per_step_ms_local = step_ms_local
+    if steps_graph is not None:
+        torch.cuda.synchronize()
+        barrier()
+        run_kernel()
+        run_comm()
+        ev0.record()
+        for i in range(args.steps):
+            run_kernel()
+            run_comm()
+        ev1.record()
+        torch.cuda.synchronize()
+        barrier()
+        graph_per_step_ms_local = ev0.elapsed_time(ev1) / args.steps
+    k_graph = steps_graph is not None
+    del graphs, steps_graph, run_kernel, run_comm, run_e2e
 
     # ---- the path's other kernels, on this workload (one GPU only) ----
     kernels = None
@@ -746,10 +783,10 @@ def main():
 
     # ---- max over ranks ----
     t = torch.tensor([step_ms_local, kern_ms_local, e2e_ms_local, hot_ms_local, float(err),
-                      period_ms_local], device=dev)
+                      period_ms_local, graph_per_step_ms_local], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, kern_ms, e2e_ms, hot_ms, err_max, period_ms = t.tolist()
+    step_ms, kern_ms, e2e_ms, hot_ms, err_max, period_ms, graph_per_step_ms = t.tolist()
 
     # ---- multi-GPU parity: O against the one-GPU decode of sampled heads ----
     parity = None
@@ -818,10 +855,16 @@ def main():
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": peak_kind, "traffic": traffic,
             "algorithmic_bytes_per_launch": local_bytes, "launch_ms": kern_ms,
-            "launch_timing": ("timed region / K: one launch per step, back to back"
+            "launch_timing": ("timed region / K: one launch per step, the K launches in one "
+                              "CUDA graph" if k_graph else
+                              "timed region / K: one launch per step, back to back"
                               if not per_step_events else
                               "mean of per-launch CUDA events inside the timed region"),
         },
+        "timed_launches": ("one CUDA graph holding the K steps, replayed once" if k_graph
+                           else "one CUDA graph replay per step" if graphs_used
+                           else "eager launches"),
+        "us_per_step_one_graph_per_step": graph_per_step_ms * 1e3 if k_graph else None,
         "cpu_baseline": cpu,
         "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "us_per_step": e2e_ms * 1e3,
