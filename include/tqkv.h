@@ -108,6 +108,13 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
  * before its first use; every decode call leaves it zeroed again (after a
  * device error, zero it again).  Calls that share one workspace must be
  * ordered (same stream, or events).
+ *
+ * A decode launch whose grid covers every SM is a programmatic dependent
+ * (cudaLaunchAttributeProgrammaticStreamSerialization): its CTAs may be
+ * dispatched while the previous kernel in the stream is finishing, and each
+ * waits for it (griddepcontrol.wait) before touching global memory, so
+ * stream order holds as for a plain launch.  Before that wait a CTA only
+ * asks L2 to prefetch the first K and V rows it is likely to stream.
  */
 size_t tqkv_decode_workspace_bytes(int B, int H, int S, int D);
 

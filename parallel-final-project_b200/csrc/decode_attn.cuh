@@ -1209,6 +1209,29 @@ __device__ __forceinline__ bool exchange_epilogue(const DecodeArgs& a, CtaCtl* c
     return true;
 }
 
+// Before its dependency wait, a CTA asks L2 for the K and V rows of the
+// first kDecodeStages tiles of chunk blockIdx.x: the first claims hand out
+// chunks 0 .. grid - 1 in about that order, so whichever CTA streams the
+// chunk finds them there.  Only a hint: it reads inputs and writes nothing,
+// and L2 serves later writes of those rows by the previous launch (a fused
+// append) like any other.
+template <int D, int BS, bool kHalfKV>
+__device__ __forceinline__ void prefetch_first_tiles(const DecodeArgs& a) {
+    using C = DecodeCfg<D, BS, kHalfKV>;
+    if (a.S <= 0 || blockIdx.x >= a.nchunks) return;
+    const long long c0 = static_cast<long long>(blockIdx.x) * a.chunk_rows;
+    if (c0 >= a.total_rows) return;
+    const long long bh = c0 / a.S;
+    const long long t0 = c0 - bh * a.S;
+    long long rows = static_cast<long long>(kDecodeStages) * C::kTile;
+    if (rows > a.S - t0) rows = a.S - t0;
+    if (c0 + rows > a.total_rows) rows = a.total_rows - c0;
+    const long long row0 = (bh / a.group) * a.S_stride + t0;
+    const uint32_t bytes = static_cast<uint32_t>(rows) * C::kRowBytes;
+    bulk_prefetch_l2(static_cast<const uint8_t*>(a.k) + row0 * C::kRowBytes, bytes);
+    bulk_prefetch_l2(static_cast<const uint8_t*>(a.v) + row0 * C::kRowBytes, bytes);
+}
+
 // ---------------------------------------------------------------------------
 constexpr int kDecodeCtasPerSm = 4;  // target residency (smem: 3 stages; regs: <= 102 per thread)
 
@@ -1232,6 +1255,14 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         ctl->abort = 0u;
         fence_barrier_init();
     }
+    // Launched as a programmatic dependent (decode launches that cover every
+    // SM are), this CTA may start while the previous launch in the stream is
+    // finishing: it lets the next launch be dispatched likewise, asks L2 for
+    // the first rows it is likely to stream, and touches no other global
+    // memory until the previous launch has completed.
+    griddep_launch_dependents();
+    if (threadIdx.x == kDecodeConsumers) prefetch_first_tiles<D, BS, kHalfKV>(a);
+    griddep_wait();
     __syncthreads();
 
     const int warp = threadIdx.x >> 5;

@@ -53,6 +53,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next launch in
+// the stream (if it was launched as a programmatic dependent) be dispatched
+// before this grid completes; wait blocks the calling thread until the grids
+// this one depends on have completed and their memory is visible.  Both do
+// nothing for a launch without that relation.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
@@ -110,6 +122,11 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// Hint: bring [src, src + bytes) into L2 (src and bytes multiples of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
