@@ -109,7 +109,7 @@ tqkv_status tqkv_kv_append(const void* x, int8_t* cache_q, void* cache_s,
  * device error, zero it again).  Calls that share one workspace must be
  * ordered (same stream, or events).
  *
- * A decode launch whose grid covers every SM is a programmatic dependent
+ * Every decode launch is a programmatic dependent
  * (cudaLaunchAttributeProgrammaticStreamSerialization): its CTAs may be
  * dispatched while the previous kernel in the stream is finishing, and each
  * waits for it (griddepcontrol.wait) before touching global memory, so

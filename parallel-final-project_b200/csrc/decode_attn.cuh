@@ -150,6 +150,9 @@ struct DecodeArgs {
     const void* k_new;         // fused append only: fp16 [BH][T_new][D], rows [S - T_new, S)
     const void* v_new;
     int T_new;
+    // the next launch in the stream may be dispatched from each CTA's start
+    // (1) or from the end of its producer's last tile (0)
+    int early_dependents;
 };
 
 template <int D, int BS, bool kHalfKV>
@@ -485,6 +488,7 @@ __device__ __forceinline__ void decode_producer(const DecodeArgs& a, uint8_t* sm
             r = head0 + t_b;
         }
     }
+    if (!a.early_dependents) griddep_launch_dependents();
     // end-of-work marker for the consumers
     if (ok) {
         if (mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
@@ -1255,12 +1259,13 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         ctl->abort = 0u;
         fence_barrier_init();
     }
-    // Launched as a programmatic dependent (decode launches that cover every
-    // SM are), this CTA may start while the previous launch in the stream is
-    // finishing: it lets the next launch be dispatched likewise, asks L2 for
-    // the first rows it is likely to stream, and touches no other global
-    // memory until the previous launch has completed.
-    griddep_launch_dependents();
+    // Launched as a programmatic dependent (decode launches are), this CTA
+    // may start while the previous launch in the stream is finishing: it
+    // lets the next launch be dispatched (here, or after its producer's last
+    // tile: early_dependents), asks L2 for the first rows it is likely to
+    // stream, and touches no other global memory until the previous launch
+    // has completed.
+    if (a.early_dependents) griddep_launch_dependents();
     if (threadIdx.x == kDecodeConsumers) prefetch_first_tiles<D, BS, kHalfKV>(a);
     griddep_wait();
     __syncthreads();

@@ -289,17 +289,19 @@ tqkv_status decode_impl(DecodeArgs a, long long total_rows, int S, int BH, void*
     a.BH = BH;
     a.max_parts = bound.max_parts;
     a.score_scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
-    // Dependent launch only when the grid covers every SM.  Measured on one
-    // B200 against plain launches, steps replayed in one graph: B4 H32 S16384
-    // (591 CTAs) 87.6-88.1 -> 84.2-84.3 us, B4 H32 S131072 617-620 -> 615 us,
-    // B8 H12 S1024 D64 (384 CTAs) 10.5 -> 10.0 us; but B2 H8 S2048 (128 CTAs)
-    // 10.3 -> 11.6 us, whose next launch sits in idle SMs for the whole of the
-    // previous one and prefetches under it.
-    if (plan.grid >= sm_count(dev))
-        return from_cuda(launch_kernel_dependent(fn, dim3(plan.grid), dim3(kDecodeThreads),
-                                                 C::kSmemBytes, stream, a));
-    return from_cuda(launch_kernel(fn, dim3(plan.grid), dim3(kDecodeThreads), C::kSmemBytes,
-                                   stream, a));
+    // Every decode launch is a programmatic dependent of the previous one.
+    // When the grid covers every SM it lets the next launch be dispatched
+    // from each CTA's start; a smaller grid does so only after each CTA's
+    // last tile is issued, because the next launch's CTAs would otherwise
+    // sit in the idle SMs through the whole launch.  Measured on one B200,
+    // steps replayed in one graph, against plain launches: B4 H32 S16384
+    // (591 CTAs) 87.6-88.1 -> 84.2-84.3 us with the early signal (85.0-85.1
+    // with the late one); B4 H32 S131072 617-620 -> 615 us; B8 H12 S1024 D64
+    // (384 CTAs) 10.5 -> 10.0 us; B2 H8 S2048 (128 CTAs) 10.3-10.7 -> 9.7-9.8
+    // us with the late signal (11.6 with the early one).
+    a.early_dependents = plan.grid >= sm_count(dev) ? 1 : 0;
+    return from_cuda(launch_kernel_dependent(fn, dim3(plan.grid), dim3(kDecodeThreads),
+                                             C::kSmemBytes, stream, a));
 }
 
 template <int D, int BS, bool kHalfKV>
